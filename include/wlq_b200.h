@@ -1,0 +1,164 @@
+/*
+ * wlq_b200.h -- C ABI of the B200 (sm_100a) WLQ 4-bit LUT linear path.
+ *
+ * Plain pointers and sizes only; no framework types.  Every GPU entry point
+ * takes device pointers and a CUDA stream (cudaStream_t, passed as an opaque
+ * pointer), validates its arguments on the host, enqueues its kernels on that
+ * stream and returns a status code; it never synchronises and never
+ * allocates device memory.  On failure wlq_last_error() returns a message for
+ * the calling thread.  Each declaration cites the reference interface it
+ * replaces (paths relative to the reference project root).
+ *
+ * Data layout (the reference's device layout, vllm_wlq/linear_method.py:326-338,
+ * 655-667):
+ *   q_packed      int32 [N * words_per_row]; 4-bit indices, 8 per word, least
+ *                 significant nibble first; words_per_row = roundup4(ceil(K/8)).
+ *   lut_c         fp16; lut_group_size == 0: [N, 16], one codebook per output
+ *                 row (the reference); lut_group_size > 0: [N, ngroups, 16]
+ *                 with column k in group (k + lut_group_offset) / lut_group_size
+ *                 and ngroups = ceil((K + lut_group_offset) / lut_group_size).
+ *   chunk_offsets int32 [N, ceil(K/512) + 1], global running offsets;
+ *   chunk_cols    uint16 [nnz], column local to its 512-wide chunk;
+ *   chunk_vals    uint8  [nnz], e5m2 byte = high byte of the fp16 value.
+ *                 Outliers REPLACE the codebook weight (all three NULL = none).
+ *   lora_B        fp16 [N, r]; lora_h / lora_H fp32 [M, r] (= A x);
+ *   dora_gamma    fp16 [N]; lora_scale = lora_alpha / r.  The DoRA term is
+ *                 applied only when lora_B, lora_h/H and dora_gamma are all
+ *                 non-NULL and r > 0 (csrc/gemv_kernel.cu:440).
+ *   x / X, out    [M, K] / [M, N], row-major, act_dtype (fp16 or bf16).
+ *
+ * out[m, n] = gamma[n] * (sum_k W[n,k] x[m,k] + s * sum_j h[m,j] B[n,j]),
+ * W the codebook weights with outliers replaced, accumulated in fp32.
+ */
+#ifndef WLQ_B200_H
+#define WLQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define WLQ_API __attribute__((visibility("default")))
+#else
+#define WLQ_API
+#endif
+
+typedef void* wlq_stream_t; /* a cudaStream_t; NULL = the legacy default stream */
+
+enum wlq_status {
+    WLQ_OK = 0,
+    WLQ_ERR_INVALID_ARG = 1, /* NULL required pointer, bad size */
+    WLQ_ERR_UNSUPPORTED = 2, /* bits / dtype / group layout this build does not run */
+    WLQ_ERR_ALIGNMENT = 3,   /* pointer not aligned as the layout requires */
+    WLQ_ERR_CUDA = 4,        /* a CUDA runtime call or launch failed */
+    WLQ_ERR_CAPACITY = 5,    /* caller's output buffer too small */
+    WLQ_ERR_DEVICE = 6       /* the current device is not sm_100 */
+};
+
+enum wlq_dtype { WLQ_DTYPE_F16 = 0, WLQ_DTYPE_BF16 = 1 };
+
+/* Message of the last failed call on this thread ("" if none). */
+WLQ_API const char* wlq_last_error(void);
+/* ABI revision of this header. */
+WLQ_API int wlq_abi_version(void);
+#define WLQ_ABI_VERSION 1
+
+/* ---------------------------------------------------------------- GPU --- */
+
+/* Decode GEMV for M = 1..16 token rows, DoRA update and outlier replacement
+ * fused.  Replaces launch_gemv_chunk_csr (csrc/gemv_kernel.cu:396-414) and
+ * gemv_forward (csrc/vllm_binding.cpp:253-315), which handle M = 1 only and
+ * need a split-K workspace; this one needs none.  bits must be 4. */
+WLQ_API int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, void* out,
+             const int32_t* chunk_offsets, const uint16_t* chunk_cols, const uint8_t* chunk_vals,
+             const void* lora_B, const float* lora_h, const void* dora_gamma, float lora_scale,
+             int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
+             int lut_group_offset, int act_dtype, wlq_stream_t stream);
+
+/* Batched forward for any M >= 1: M <= 16 runs the GEMV-class kernel, larger
+ * M the tcgen05 tensor-core GEMM with dequantisation, outlier replacement and
+ * the DoRA epilogue fused.  Replaces launch_gemm_metalog_dora
+ * (csrc/gemm_kernel.cu:527-547) and the M >= 16 dequantise + cuBLAS +
+ * epilogue composition of gemm_forward (csrc/vllm_binding.cpp:318-419). */
+WLQ_API int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* out,
+             const int32_t* chunk_offsets, const uint16_t* chunk_cols, const uint8_t* chunk_vals,
+             const float* lora_H, const void* lora_B, const void* dora_gamma, float lora_scale,
+             int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
+             int lut_group_offset, int act_dtype, wlq_stream_t stream);
+
+/* Dense fp16 W[N, K] (codebook gather, then outliers overwritten), bit-exact
+ * with the reference.  bits 1..4.  Replaces launch_dequant_patch_metalog
+ * (csrc/gemm_kernel.cu:475-489) and dequant_w0 (csrc/vllm_binding.cpp:421-453). */
+WLQ_API int wlq_dequant(const int32_t* q_packed, const void* lut_c, void* W_out,
+                const int32_t* chunk_offsets, const uint16_t* chunk_cols, const uint8_t* chunk_vals,
+                int N, int K, int bits, int words_per_row, int lut_group_size, int lut_group_offset,
+                wlq_stream_t stream);
+
+/* Kept for interface parity with init_workspaces (csrc/vllm_binding.cpp:241-251):
+ * the kernels of this library need no workspace, so this only validates. */
+WLQ_API int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device);
+
+/* ---------------------------------------------------------------- CPU --- */
+/* Load-time codecs (host memory). */
+
+/* roundup4(ceil(K / symbols_per_word)) (vllm_wlq/linear_method.py:326-331). */
+WLQ_API int64_t wlq_words_per_row(int64_t K, int bits);
+
+/* Continuous on-disk index stream -> row-aligned words [N * words_per_row];
+ * symbols beyond n_src words read as 0.  Replaces repack_q_indices_row_aligned
+ * (csrc/vllm_binding.cpp:198-236). */
+WLQ_API int wlq_repack_q_indices_row_aligned(const int32_t* src, int64_t n_src, int64_t N, int64_t K,
+                                     int bits, int32_t* dst, int64_t dst_capacity,
+                                     int64_t* words_per_row);
+
+/* Rows [r0,r1) x columns [c0,c1) of a continuous [N_full, K_full] index stream
+ * -> row-aligned words: the tensor-parallel shard of a layer.  Replaces the
+ * unpack / slice / pack sequence of vllm_wlq/linear_method.py:724, 753-761, 792. */
+WLQ_API int wlq_repack_q_indices_slice(const int32_t* src, int64_t n_src, int64_t N_full, int64_t K_full, int bits,
+                               int64_t r0, int64_t r1, int64_t c0, int64_t c1, int32_t* dst,
+                               int64_t dst_capacity, int64_t* words_per_row);
+
+/* Elias-Fano tiles -> sorted, unique flat outlier positions r*K + c, the
+ * row-major order of the outlier value list; positions may be NULL to count.
+ * Replaces decode_elias_fano (vllm_wlq/linear_method.py:243-281) where the
+ * mask is needed for tensor-parallel slicing. */
+WLQ_API int wlq_decode_ef_positions(const int64_t* tile_meta, int64_t n_tiles, const int32_t* bitstream,
+                            int64_t n_words, int64_t N, int64_t K, int64_t tile_size, int64_t* positions,
+                            int64_t capacity, int64_t* count);
+
+/* Sorted unique flat positions -> chunk-CSR (vllm_wlq/linear_method.py:284-303). */
+WLQ_API int wlq_positions_to_chunk_csr(const int64_t* positions, int64_t n, int64_t N, int64_t K, int64_t chunk_m,
+                               int32_t* offsets, uint16_t* cols);
+
+/* Elias-Fano tiles -> chunk-CSR.  offsets [N, ceil(K/chunk_m)+1]; cols may be
+ * NULL to count only (nnz returned either way).  Replaces
+ * decode_ef_to_chunk_csr (csrc/vllm_binding.cpp:94-196). */
+WLQ_API int wlq_decode_ef_to_chunk_csr(const int64_t* tile_meta, int64_t n_tiles, const int32_t* bitstream,
+                               int64_t n_words, int64_t N, int64_t K, int64_t tile_size,
+                               int64_t chunk_m, int32_t* offsets, uint16_t* cols,
+                               int64_t cols_capacity, int64_t* nnz);
+
+/* Dense outlier mask [N, K] (0/1 bytes) -> chunk-CSR.  Replaces
+ * build_chunk_csr (vllm_wlq/linear_method.py:284-312). */
+WLQ_API int wlq_build_chunk_csr(const uint8_t* mask, int64_t N, int64_t K, int64_t chunk_m,
+                        int32_t* offsets, uint16_t* cols, int64_t cols_capacity, int64_t* nnz);
+
+/* fp16 outlier values -> e5m2 bytes, (u16 + 0x80) >> 8 clamped
+ * (vllm_wlq/linear_method.py:306-308, 519-521). */
+WLQ_API int wlq_fp16_to_fp8_bytes(const uint16_t* src, int64_t n, uint8_t* dst);
+
+/* Host twin of wlq_dequant, for loading without a GPU (the reference's
+ * gather fallback, vllm_wlq/linear_method.py:608-623). */
+WLQ_API int wlq_dequant_host(const int32_t* q_packed, const uint16_t* lut_c, uint16_t* W_out,
+                     const int32_t* chunk_offsets, const uint16_t* chunk_cols,
+                     const uint8_t* chunk_vals, int64_t N, int64_t K, int bits,
+                     int64_t words_per_row, int64_t lut_group_size, int64_t lut_group_offset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WLQ_B200_H */

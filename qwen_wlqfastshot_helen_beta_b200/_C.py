@@ -1,0 +1,300 @@
+"""The reference's ``vllm_wlq._C`` module surface over this package's C ABI.
+
+Same function names, argument order and meaning as the pybind module of
+csrc/vllm_binding.cpp:455-532 (``gemv_forward``, ``gemm_forward``,
+``dequant_w0``, ``decode_ef_to_chunk_csr``, ``repack_q_indices_row_aligned``,
+``init_workspaces``), each implemented by one call into libwlq_b200.so.  Like
+the reference, optional tensors that are ``None`` or empty are absent, the
+GPU functions launch on the current CUDA stream and raise ``RuntimeError`` on
+bad input.  Two trailing keyword arguments select per-group codebooks
+(``lut_group_size`` / ``lut_group_offset``, 0 = one codebook per row as in the
+reference).  The GPU functions accept fp16 (as the reference) or bf16
+activations; ``out`` must have the activation dtype.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import numpy as np
+import torch
+
+from ._lib import WLQ_DTYPE_BF16, WLQ_DTYPE_F16, check, lib
+
+_NONE = None
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _opt(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    """None / undefined / empty -> None (csrc/vllm_binding.cpp:272-286)."""
+    if t is None or t.numel() == 0:
+        return None
+    return t
+
+
+def words_per_row(K: int, bits: int) -> int:
+    return int(lib.wlq_words_per_row(int(K), int(bits)))
+
+
+def _act_dtype(t: torch.Tensor) -> int:
+    if t.dtype == torch.float16:
+        return WLQ_DTYPE_F16
+    if t.dtype == torch.bfloat16:
+        return WLQ_DTYPE_BF16
+    raise RuntimeError(f"wlq: activations must be float16 or bfloat16, got {t.dtype}")
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(f"wlq: {msg}")
+
+
+def _check_common(name, tensors, required):
+    for nm, t in zip(required, tensors):
+        _require(t is not None, f"{name}: {nm} is required")
+        _require(t.is_cuda, f"{name}: {nm} must be a CUDA tensor")
+        _require(t.is_contiguous(), f"{name}: {nm} must be contiguous")
+
+
+def _check_opt(name, nm, t, dtype, device):
+    if t is None:
+        return
+    _require(t.is_cuda and t.device == device, f"{name}: {nm} must be on {device}")
+    _require(t.is_contiguous(), f"{name}: {nm} must be contiguous")
+    _require(t.dtype == dtype, f"{name}: {nm} must be {dtype}, got {t.dtype}")
+
+
+def _linear_checks(name, x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lora_B, lora_h, gamma,
+                   group_size, group_offset):
+    _check_common(name, (q_packed, lut_c, x, out), ("q_packed", "lut_c", "x", "out"))
+    dev = x.device
+    for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("out", out)):
+        _require(t.device == dev, f"{name}: {nm} must be on {dev}")
+    _require(q_packed.dtype == torch.int32, f"{name}: q_packed must be int32")
+    _require(lut_c.dtype == torch.float16, f"{name}: lut_c must be float16")
+    _require(out.dtype == x.dtype, f"{name}: out dtype {out.dtype} must match x dtype {x.dtype}")
+    _require(K > 0 and x.numel() % K == 0, f"{name}: x has {x.numel()} elements, not a multiple of K={K}")
+    M = x.numel() // K
+    _require(out.numel() == M * N, f"{name}: out has {out.numel()} elements, expected {M}x{N}")
+    _require(q_packed.numel() >= N * wpr, f"{name}: q_packed has {q_packed.numel()} words, need {N}x{wpr}")
+    ng = (K + group_offset + group_size - 1) // group_size if group_size > 0 else 1
+    kcb = 1 << bits
+    _require(lut_c.numel() == N * ng * kcb,
+             f"{name}: lut_c has {lut_c.numel()} entries, expected {N}x{ng}x{kcb} (group_size={group_size})")
+    if offs is not None and cols is not None and vals is not None:
+        chunk_m = 640 if bits == 3 else 512
+        nc = (K + chunk_m - 1) // chunk_m
+        _check_opt(name, "chunk_offsets", offs, torch.int32, dev)
+        _check_opt(name, "chunk_cols", cols, torch.uint16, dev)
+        _check_opt(name, "chunk_vals", vals, torch.uint8, dev)
+        _require(offs.numel() == N * (nc + 1), f"{name}: chunk_offsets must be [{N}, {nc + 1}]")
+        _require(cols.numel() == vals.numel(), f"{name}: chunk_cols and chunk_vals lengths differ")
+    r = 0
+    if lora_B is not None and lora_h is not None and gamma is not None:
+        _check_opt(name, "lora_B", lora_B, torch.float16, dev)
+        _check_opt(name, "lora_h", lora_h, torch.float32, dev)
+        _check_opt(name, "dora_gamma", gamma, torch.float16, dev)
+        r = int(lora_B.size(1)) if lora_B.dim() > 1 else 0
+        _require(lora_B.numel() == N * r, f"{name}: lora_B must be [{N}, r]")
+        _require(lora_h.numel() == M * r, f"{name}: lora_h must hold {M}x{r} values")
+        _require(gamma.numel() == N, f"{name}: dora_gamma must have {N} values")
+    return M, r
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+class _DeviceGuard:
+    """Makes `dev` the current CUDA device for the duration of a call (the C
+    ABI launches on the current device)."""
+
+    __slots__ = ("dev", "prev")
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.dev:
+            self.prev = cur
+            torch.cuda.set_device(self.dev)
+
+    def __exit__(self, *a):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+def gemv_forward(q_packed, lut_c, x, out, N, K, bits, chunk_offsets=None, chunk_cols=None, chunk_vals=None,
+                 lora_B=None, lora_h=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
+                 lut_group_offset=0):
+    """Decode GEMV, M = x.numel() / K <= 16 (csrc/vllm_binding.cpp:253-315)."""
+    N, K, bits = int(N), int(K), int(bits)
+    offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
+    lb, lh, gm = _opt(lora_B), _opt(lora_h), _opt(dora_gamma)
+    wpr = words_per_row(K, bits)
+    M, r = _linear_checks("gemv_forward", x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lb, lh, gm,
+                          int(lut_group_size), int(lut_group_offset))
+    with _DeviceGuard(x.device):
+        rc = lib.wlq_gemv(_ptr(q_packed), _ptr(lut_c), _ptr(x), _ptr(out), _ptr(offs), _ptr(cols), _ptr(vals),
+                          _ptr(lb), _ptr(lh), _ptr(gm), float(lora_scale), r, M, N, K, bits, wpr,
+                          int(lut_group_size), int(lut_group_offset), _act_dtype(x), _stream(x.device))
+    check(rc, "wlq_gemv")
+
+
+def gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,
+                 chunk_vals=None, lora_H=None, lora_B=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
+                 lut_group_offset=0):
+    """Batched forward for any M (csrc/vllm_binding.cpp:318-419)."""
+    N, K, bits, wpr = int(N), int(K), int(bits), int(words_per_row)
+    offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
+    lb, lh, gm = _opt(lora_B), _opt(lora_H), _opt(dora_gamma)
+    M, r = _linear_checks("gemm_forward", X, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lb, lh, gm,
+                          int(lut_group_size), int(lut_group_offset))
+    with _DeviceGuard(X.device):
+        rc = lib.wlq_gemm(_ptr(X), _ptr(q_packed), _ptr(lut_c), _ptr(out), _ptr(offs), _ptr(cols), _ptr(vals),
+                          _ptr(lh), _ptr(lb), _ptr(gm), float(lora_scale), r, M, N, K, bits, wpr,
+                          int(lut_group_size), int(lut_group_offset), _act_dtype(X), _stream(X.device))
+    check(rc, "wlq_gemm")
+
+
+def dequant_w0(q_packed, lut_c, W_out, N, K, bits, words_per_row, chunk_offsets, chunk_cols, chunk_vals,
+               lut_group_size=0, lut_group_offset=0):
+    """Dense fp16 W = codebook[q] with outliers replaced, bit-exact
+    (csrc/vllm_binding.cpp:421-453).  CUDA tensors run the GPU kernel; CPU
+    tensors the host codec (load time without a GPU)."""
+    N, K, bits, wpr = int(N), int(K), int(bits), int(words_per_row)
+    offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
+    _require(W_out.dtype == torch.float16 and W_out.is_contiguous() and W_out.numel() == N * K,
+             "dequant_w0: W_out must be a contiguous float16 [N, K] tensor")
+    _require(q_packed.dtype == torch.int32 and lut_c.dtype == torch.float16, "dequant_w0: q int32, lut fp16")
+    _require(q_packed.is_contiguous() and lut_c.is_contiguous(), "dequant_w0: inputs must be contiguous")
+    if W_out.is_cuda:
+        for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("chunk_offsets", offs), ("chunk_cols", cols),
+                      ("chunk_vals", vals)):
+            _require(t is None or (t.is_cuda and t.device == W_out.device and t.is_contiguous()),
+                     f"dequant_w0: {nm} must be a contiguous tensor on {W_out.device}")
+        with _DeviceGuard(W_out.device):
+            rc = lib.wlq_dequant(_ptr(q_packed), _ptr(lut_c), _ptr(W_out), _ptr(offs), _ptr(cols), _ptr(vals),
+                                 N, K, bits, wpr, int(lut_group_size), int(lut_group_offset),
+                                 _stream(W_out.device))
+        check(rc, "wlq_dequant")
+        return
+    for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("chunk_offsets", offs), ("chunk_cols", cols),
+                  ("chunk_vals", vals)):
+        _require(t is None or (not t.is_cuda and t.is_contiguous()), f"dequant_w0: {nm} must be a CPU tensor")
+    rc = lib.wlq_dequant_host(_ptr(q_packed), _ptr(lut_c), _ptr(W_out), _ptr(offs), _ptr(cols), _ptr(vals),
+                              N, K, bits, wpr, int(lut_group_size), int(lut_group_offset))
+    check(rc, "wlq_dequant_host")
+
+
+def init_workspaces(max_N, max_K, device):
+    """Interface parity with csrc/vllm_binding.cpp:241-251; no workspace is needed."""
+    dev = torch.device(device)
+    check(lib.wlq_init_workspaces(int(max_N), int(max_K), dev.index or 0), "wlq_init_workspaces")
+
+
+# ----------------------------------------------------------------- codecs ---
+
+def _cpu_i32(t: torch.Tensor) -> torch.Tensor:
+    t = t.detach().to("cpu").contiguous()
+    if t.dtype != torch.int32:
+        t = t.view(torch.int32) if t.element_size() == 4 else t.to(torch.int32)
+    return t
+
+
+def repack_q_indices_row_aligned(q_packed_raw, N, K, bits) -> Tuple[torch.Tensor, int]:
+    """Continuous stream -> row-aligned int32 words (csrc/vllm_binding.cpp:198-236)."""
+    src = _cpu_i32(q_packed_raw)
+    wpr = words_per_row(K, bits)
+    out = torch.zeros(int(N) * wpr, dtype=torch.int32)
+    w = ctypes.c_int64(0)
+    check(lib.wlq_repack_q_indices_row_aligned(_ptr(src), src.numel(), int(N), int(K), int(bits), _ptr(out),
+                                                out.numel(), ctypes.byref(w)), "wlq_repack_q_indices_row_aligned")
+    return out, int(w.value)
+
+
+def repack_q_indices_slice(q_packed_raw, N_full, K_full, bits, r0, r1, c0, c1) -> Tuple[torch.Tensor, int]:
+    """Rows [r0,r1) x cols [c0,c1) of a continuous stream -> row-aligned words."""
+    src = _cpu_i32(q_packed_raw)
+    wpr = words_per_row(int(c1) - int(c0), bits)
+    out = torch.zeros((int(r1) - int(r0)) * wpr, dtype=torch.int32)
+    w = ctypes.c_int64(0)
+    check(lib.wlq_repack_q_indices_slice(_ptr(src), src.numel(), int(N_full), int(K_full), int(bits), int(r0),
+                                          int(r1), int(c0), int(c1), _ptr(out), out.numel(), ctypes.byref(w)),
+          "wlq_repack_q_indices_slice")
+    return out, int(w.value)
+
+
+def decode_ef_to_chunk_csr(ef_tile_meta, ef_bitstream, N, K, tile_size, chunk_m):
+    """EF tiles -> (chunk_offsets int32 [N, nc+1], chunk_cols uint16) (csrc/vllm_binding.cpp:94-196)."""
+    meta = ef_tile_meta.detach().to("cpu", torch.int64).contiguous()
+    bs = _cpu_i32(ef_bitstream)
+    N, K, tile_size, chunk_m = int(N), int(K), int(tile_size), int(chunk_m)
+    nc = (K + chunk_m - 1) // chunk_m
+    offs = torch.zeros((N, nc + 1), dtype=torch.int32)
+    nnz = ctypes.c_int64(0)
+    n_tiles = meta.numel() // 2
+    check(lib.wlq_decode_ef_to_chunk_csr(_ptr(meta), n_tiles, _ptr(bs), bs.numel(), N, K, tile_size, chunk_m,
+                                         _ptr(offs), None, 0, ctypes.byref(nnz)), "wlq_decode_ef_to_chunk_csr")
+    cols = torch.empty(int(nnz.value), dtype=torch.uint16)
+    check(lib.wlq_decode_ef_to_chunk_csr(_ptr(meta), n_tiles, _ptr(bs), bs.numel(), N, K, tile_size, chunk_m,
+                                         _ptr(offs), _ptr(cols), cols.numel(), ctypes.byref(nnz)),
+          "wlq_decode_ef_to_chunk_csr")
+    return offs, cols
+
+
+def decode_ef_positions(ef_tile_meta, ef_bitstream, N, K, tile_size) -> np.ndarray:
+    """EF tiles -> sorted flat outlier positions r*K + c (int64 numpy)."""
+    meta = ef_tile_meta.detach().to("cpu", torch.int64).contiguous()
+    bs = _cpu_i32(ef_bitstream)
+    cnt = ctypes.c_int64(0)
+    n_tiles = meta.numel() // 2
+    check(lib.wlq_decode_ef_positions(_ptr(meta), n_tiles, _ptr(bs), bs.numel(), int(N), int(K), int(tile_size),
+                                      None, 0, ctypes.byref(cnt)), "wlq_decode_ef_positions")
+    pos = torch.empty(int(cnt.value), dtype=torch.int64)
+    check(lib.wlq_decode_ef_positions(_ptr(meta), n_tiles, _ptr(bs), bs.numel(), int(N), int(K), int(tile_size),
+                                      _ptr(pos), pos.numel(), ctypes.byref(cnt)), "wlq_decode_ef_positions")
+    return pos.numpy()
+
+
+def positions_to_chunk_csr(positions, N, K, chunk_m):
+    """Sorted flat positions -> (chunk_offsets, chunk_cols) (vllm_wlq/linear_method.py:284-303)."""
+    pos = torch.as_tensor(np.ascontiguousarray(positions, dtype=np.int64))
+    N, K, chunk_m = int(N), int(K), int(chunk_m)
+    nc = (K + chunk_m - 1) // chunk_m
+    offs = torch.zeros((N, nc + 1), dtype=torch.int32)
+    cols = torch.empty(pos.numel(), dtype=torch.uint16)
+    check(lib.wlq_positions_to_chunk_csr(_ptr(pos), pos.numel(), N, max(K, 1), chunk_m, _ptr(offs), _ptr(cols)),
+          "wlq_positions_to_chunk_csr")
+    return offs, cols
+
+
+def build_chunk_csr_from_mask(mask, chunk_m):
+    """Dense bool mask [N, K] -> (chunk_offsets, chunk_cols) (vllm_wlq/linear_method.py:284-303)."""
+    m = np.ascontiguousarray(np.asarray(mask), dtype=np.uint8)
+    N, K = m.shape
+    nc = (K + chunk_m - 1) // chunk_m
+    offs = torch.zeros((N, nc + 1), dtype=torch.int32)
+    nnz = ctypes.c_int64(0)
+    mp = ctypes.c_void_p(m.ctypes.data)
+    check(lib.wlq_build_chunk_csr(mp, N, K, int(chunk_m), _ptr(offs), None, 0, ctypes.byref(nnz)),
+          "wlq_build_chunk_csr")
+    cols = torch.empty(int(nnz.value), dtype=torch.uint16)
+    check(lib.wlq_build_chunk_csr(mp, N, K, int(chunk_m), _ptr(offs), _ptr(cols), cols.numel(), ctypes.byref(nnz)),
+          "wlq_build_chunk_csr")
+    return offs, cols
+
+
+def fp16_to_fp8_bytes(vals: torch.Tensor) -> torch.Tensor:
+    """fp16 outlier values -> e5m2 bytes (vllm_wlq/linear_method.py:306-308)."""
+    v = vals.detach().to("cpu").contiguous()
+    if v.dtype != torch.float16:
+        raise RuntimeError("fp16_to_fp8_bytes: expects float16 values")
+    out = torch.empty(v.numel(), dtype=torch.uint8)
+    check(lib.wlq_fp16_to_fp8_bytes(_ptr(v), v.numel(), _ptr(out)), "wlq_fp16_to_fp8_bytes")
+    return out

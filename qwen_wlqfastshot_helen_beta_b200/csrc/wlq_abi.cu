@@ -1,0 +1,190 @@
+// extern "C" entry points of libwlq_b200.so: argument validation, error
+// reporting and dispatch to the sm_100a kernels.  Mirrors the checks and the
+// optional-argument handling of csrc/vllm_binding.cpp:253-453 (NULL = absent,
+// chunk_m from bits) and adds the dtype / alignment / shape checks that the
+// reference leaves to the caller.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "wlq_common.cuh"
+#include "wlq_internal.h"
+
+namespace wlq {
+
+static thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return WLQ_OK;
+    return fail(WLQ_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+namespace {
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];
+int g_cc_major[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+
+int current_device(int* dev) {
+    const cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return check_cuda(e, "cudaGetDevice");
+    if (*dev < 0 || *dev >= kMaxDevices) return fail(WLQ_ERR_DEVICE, "device index %d out of range", *dev);
+    std::call_once(g_dev_once[*dev], [d = *dev]() {
+        cudaDeviceGetAttribute(&g_sm_count[d], cudaDevAttrMultiProcessorCount, d);
+        cudaDeviceGetAttribute(&g_cc_major[d], cudaDevAttrComputeCapabilityMajor, d);
+    });
+    return WLQ_OK;
+}
+
+int require_sm100() {
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    if (g_cc_major[dev] != 10)
+        return fail(WLQ_ERR_DEVICE, "device %d has compute capability %d.x; this build runs sm_100a only", dev,
+                    g_cc_major[dev]);
+    return WLQ_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Shared validation of the quantized-linear arguments.
+int build_args(const char* fn, const void* x, const int32_t* q, const void* lut, void* out,
+               const int32_t* off, const uint16_t* ccols, const uint8_t* cvals, const void* loraB,
+               const float* lorah, const void* gamma, float scale, int r, int M, int N, int K, int bits,
+               int wpr, int G, int goff, int dtype, LinearArgs& a) {
+    if (M < 0 || N < 0 || K < 0) return fail(WLQ_ERR_INVALID_ARG, "%s: negative size (M=%d N=%d K=%d)", fn, M, N, K);
+    if (bits != 4)
+        return fail(WLQ_ERR_UNSUPPORTED, "%s: only 4-bit indices are supported by the fused kernels (bits=%d)", fn, bits);
+    if (dtype != WLQ_DTYPE_F16 && dtype != WLQ_DTYPE_BF16)
+        return fail(WLQ_ERR_UNSUPPORTED, "%s: act_dtype must be WLQ_DTYPE_F16 or WLQ_DTYPE_BF16 (got %d)", fn, dtype);
+    if (M > 0 && N > 0 && K > 0 && (!x || !q || !lut || !out))
+        return fail(WLQ_ERR_INVALID_ARG, "%s: x, q_packed, lut_c and out are required", fn);
+    const int64_t need_wpr = words_per_row(K, bits);
+    if (wpr != need_wpr)
+        return fail(WLQ_ERR_INVALID_ARG, "%s: words_per_row=%d but K=%d needs %lld (row-aligned layout)", fn, wpr, K,
+                    (long long)need_wpr);
+    if (G < 0 || goff < 0 || (G > 0 && goff >= G))
+        return fail(WLQ_ERR_INVALID_ARG, "%s: bad codebook grouping (group_size=%d, group_offset=%d)", fn, G, goff);
+    if (!aligned(q, 16) || !aligned(lut, 16))
+        return fail(WLQ_ERR_ALIGNMENT, "%s: q_packed and lut_c must be 16-byte aligned", fn);
+    if (!aligned(x, 2) || !aligned(out, 2)) return fail(WLQ_ERR_ALIGNMENT, "%s: x/out must be 2-byte aligned", fn);
+    const bool has_outl = off && ccols && cvals;
+    const bool dora = loraB && lorah && gamma && r > 0;
+    a.q = reinterpret_cast<const uint32_t*>(q);
+    a.lut = reinterpret_cast<const uint16_t*>(lut);
+    a.x = x;
+    a.out = out;
+    a.off = has_outl ? off : nullptr;
+    a.ccols = has_outl ? ccols : nullptr;
+    a.cvals = has_outl ? cvals : nullptr;
+    a.loraB = dora ? reinterpret_cast<const uint16_t*>(loraB) : nullptr;
+    a.lorah = dora ? lorah : nullptr;
+    a.gamma = dora ? reinterpret_cast<const uint16_t*>(gamma) : nullptr;
+    a.scale = scale;
+    a.r = dora ? r : 0;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.wpr = wpr;
+    a.group_size = G;
+    a.group_offset = goff;
+    a.ngroups = G > 0 ? (K + goff + G - 1) / G : 1;
+    a.chunk_m = chunk_m_for_bits(bits);
+    a.ncsr = (K + a.chunk_m - 1) / a.chunk_m;
+    a.dtype = dtype;
+    return WLQ_OK;
+}
+}  // namespace
+
+int device_sm_count() {
+    int dev = 0;
+    if (current_device(&dev) != WLQ_OK) return 148;
+    return g_sm_count[dev] > 0 ? g_sm_count[dev] : 148;
+}
+
+}  // namespace wlq
+
+using namespace wlq;
+
+extern "C" {
+
+const char* wlq_last_error(void) { return g_last_error; }
+
+int wlq_abi_version(void) { return WLQ_ABI_VERSION; }
+
+int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, void* out, const int32_t* chunk_offsets,
+             const uint16_t* chunk_cols, const uint8_t* chunk_vals, const void* lora_B, const float* lora_h,
+             const void* dora_gamma, float lora_scale, int r, int M, int N, int K, int bits, int words_per_row,
+             int lut_group_size, int lut_group_offset, int act_dtype, wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    LinearArgs a;
+    int rc = build_args("wlq_gemv", x, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_h,
+                        dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size, lut_group_offset,
+                        act_dtype, a);
+    if (rc) return rc;
+    if (M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: M must be 1..16 (got %d); use wlq_gemm", M);
+    if (M == 0 || N == 0) return WLQ_OK;
+    if ((rc = require_sm100())) return rc;
+    return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* out, const int32_t* chunk_offsets,
+             const uint16_t* chunk_cols, const uint8_t* chunk_vals, const float* lora_H, const void* lora_B,
+             const void* dora_gamma, float lora_scale, int r, int M, int N, int K, int bits, int words_per_row,
+             int lut_group_size, int lut_group_offset, int act_dtype, wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    LinearArgs a;
+    int rc = build_args("wlq_gemm", X, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_H,
+                        dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size, lut_group_offset,
+                        act_dtype, a);
+    if (rc) return rc;
+    if (M == 0 || N == 0) return WLQ_OK;
+    if ((rc = require_sm100())) return rc;
+    if (M <= 16) return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
+    return launch_gemm(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wlq_dequant(const int32_t* q_packed, const void* lut_c, void* W_out, const int32_t* chunk_offsets,
+                const uint16_t* chunk_cols, const uint8_t* chunk_vals, int N, int K, int bits, int words_per_row,
+                int lut_group_size, int lut_group_offset, wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    if (N < 0 || K < 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_dequant: negative size");
+    if (bits < 1 || bits > 4) return fail(WLQ_ERR_UNSUPPORTED, "wlq_dequant: bits must be 1..4 (got %d)", bits);
+    if (N == 0 || K == 0) return WLQ_OK;
+    if (!q_packed || !lut_c || !W_out) return fail(WLQ_ERR_INVALID_ARG, "wlq_dequant: q_packed, lut_c, W_out required");
+    if (words_per_row != wlq::words_per_row(K, bits))
+        return fail(WLQ_ERR_INVALID_ARG, "wlq_dequant: words_per_row=%d does not match K=%d, bits=%d", words_per_row, K,
+                    bits);
+    if (lut_group_size < 0 || lut_group_offset < 0 || (lut_group_size > 0 && lut_group_offset >= lut_group_size))
+        return fail(WLQ_ERR_INVALID_ARG, "wlq_dequant: bad codebook grouping");
+    if (!aligned(q_packed, 4) || !aligned(lut_c, 2) || !aligned(W_out, 2))
+        return fail(WLQ_ERR_ALIGNMENT, "wlq_dequant: misaligned pointer");
+    int rc = require_sm100();
+    if (rc) return rc;
+    const bool has_outl = chunk_offsets && chunk_cols && chunk_vals;
+    const int chunk_m = chunk_m_for_bits(bits);
+    const int ngroups = lut_group_size > 0 ? (K + lut_group_offset + lut_group_size - 1) / lut_group_size : 1;
+    return launch_dequant(reinterpret_cast<const uint32_t*>(q_packed), reinterpret_cast<const uint16_t*>(lut_c),
+                          reinterpret_cast<uint16_t*>(W_out), has_outl ? chunk_offsets : nullptr,
+                          has_outl ? chunk_cols : nullptr, has_outl ? chunk_vals : nullptr, N, K, bits, words_per_row,
+                          lut_group_size, lut_group_offset, ngroups, chunk_m, (K + chunk_m - 1) / chunk_m,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device) {
+    g_last_error[0] = '\0';
+    if (max_N < 0 || max_K < 0 || device < 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_init_workspaces: bad arguments");
+    return WLQ_OK;
+}
+
+}  // extern "C"

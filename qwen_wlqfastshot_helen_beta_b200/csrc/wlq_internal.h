@@ -1,0 +1,50 @@
+// Host-side plumbing shared by the translation units of libwlq_b200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/wlq_b200.h"
+
+namespace wlq {
+
+// Records `msg` as this thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Maps a CUDA error to WLQ_ERR_CUDA with its name, or returns WLQ_OK.
+int check_cuda(cudaError_t e, const char* what);
+
+// Arguments of one quantized-linear call, already validated.
+struct LinearArgs {
+    const uint32_t* q;       // [N * wpr]
+    const uint16_t* lut;     // fp16 bits, [N, ngroups, 16]
+    const void* x;           // [M, K] act dtype
+    void* out;               // [M, N] act dtype
+    const int32_t* off;      // [N, ncsr + 1] or null
+    const uint16_t* ccols;   // [nnz] or null
+    const uint8_t* cvals;    // [nnz] or null
+    const uint16_t* loraB;   // fp16 [N, r] or null
+    const float* lorah;      // fp32 [M, r] or null
+    const uint16_t* gamma;   // fp16 [N] or null
+    float scale;
+    int r;                   // 0 when the DoRA term is off
+    int M, N, K;
+    int wpr;
+    int group_size;          // 0 = one codebook per row
+    int group_offset;
+    int ngroups;             // codebooks per row
+    int chunk_m;             // outlier chunk width (512 for 4-bit)
+    int ncsr;                // outlier chunks per row
+    int dtype;               // WLQ_DTYPE_*
+};
+
+int launch_gemv(const LinearArgs& a, cudaStream_t stream);
+int launch_gemm(const LinearArgs& a, cudaStream_t stream);
+int launch_dequant(const uint32_t* q, const uint16_t* lut, uint16_t* W, const int32_t* off,
+                   const uint16_t* ccols, const uint8_t* cvals, int N, int K, int bits, int wpr,
+                   int group_size, int group_offset, int ngroups, int chunk_m, int ncsr,
+                   cudaStream_t stream);
+
+// Multiprocessor count of the current device (cached per device).
+int device_sm_count();
+
+}  // namespace wlq
