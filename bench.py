@@ -1,0 +1,539 @@
+"""Benchmark of the WLQ 4-bit LUT decode GEMV on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (config 1): the four Qwen2.5-7B linears -- qkv 3584->4608, o
+3584->3584, gate_up 3584->37888, down 18944->3584 -- at decode batch
+M in {1, 4, 8, 16}, bf16 activations, benchmark quantisation recipe (one
+16-entry fp16 codebook per row and 128 columns, DoRA rank 16, 0.5% outliers),
+seeded synthetic weights and activations.  One step = the 16 (linear, M)
+forward calls, each through the C ABI entry point wlq_gemm, on one of several
+rotating weight copies whose total exceeds the 126 MB L2 (inputs larger than
+L2; no flush needed).
+
+Metric: algorithmic bytes (indices, codebooks, outlier CSR, DoRA tensors,
+activations, outputs) / time, in GB/s, whole job.  ``value`` times K steps of
+a CUDA graph of the step with inputs resident in HBM; ``roofline`` divides the
+same bytes by the summed kernel-only durations (CUDA events recorded between
+the kernels inside the graph) and by the measured HBM copy bandwidth; ``e2e``
+times K steps through the public op with host (pinned) activations copied in
+and outputs copied out every step.
+
+With --gpus N > 1 (torchrun, one rank per GPU) the linears are sharded the way
+vLLM tensor parallelism shards them (qkv/gate_up by output rows, o/down by
+input columns, the latter followed by an NCCL all-reduce of [M, hidden]);
+value = bytes of the whole layer / max-over-ranks time (strong scaling).
+
+--impl reference times the reference's CPU dequantize-then-matmul path
+(oracle/cpu_baseline.py) on the host cores on the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "W4-LUT GEMV GB/s vs HBM peak; GEMM TFLOPS; Qwen2.5-7B decode tok/s"
+SHAPES = [("qkv", 3584, 4608), ("o", 3584, 3584), ("gate_up", 3584, 37888), ("down", 18944, 3584)]
+MS = [1, 4, 8, 16]
+GROUP = 128
+RANK = 16
+DENSITY = 0.005
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": FALLBACK_HBM_GBS}, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period, self.stop_evt, self.thread = period_s, threading.Event(), None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _sample(self):
+        try:
+            self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+            mask = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for bit, name in self.REASONS.items():
+                if mask & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self.stop_evt.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nvml:
+            self._sample()
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.nvml:
+            self.stop_evt.set()
+            self.thread.join()
+            self._sample()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------- graph event nodes
+
+class GraphEvents:
+    """Timing events that can be recorded inside a captured CUDA graph
+    (cudaEventRecordWithFlags with cudaEventRecordExternal)."""
+
+    def __init__(self):
+        import torch
+        self.torch = torch
+        self.rt = None
+        for name in ("libcudart.so.12", "libcudart.so"):
+            try:
+                self.rt = ctypes.CDLL(name)
+                break
+            except OSError:
+                continue
+        if self.rt is not None:
+            self.rt.cudaEventRecordWithFlags.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint]
+            self.rt.cudaEventRecordWithFlags.restype = ctypes.c_int
+
+    def record(self, ev):
+        stream = self.torch.cuda.current_stream()
+        if self.rt is None:
+            ev.record(stream)
+            return
+        rc = self.rt.cudaEventRecordWithFlags(ctypes.c_void_p(ev.cuda_event), ctypes.c_void_p(stream.cuda_stream), 1)
+        if rc != 0:
+            raise RuntimeError(f"cudaEventRecordWithFlags failed: {rc}")
+
+
+# ------------------------------------------------------------ workloads
+
+def build_layers(copies, rank, world, device, seed0=1000):
+    """copies x 4 linears (the rank's tensor-parallel shard of each)."""
+    import torch
+    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+    layers = []
+    for c in range(copies):
+        row = {}
+        for si, (name, K, N) in enumerate(SHAPES):
+            seed = seed0 + 97 * c + si
+            if world > 1 and name in ("qkv", "gate_up"):
+                Np = N // world
+                L = S.make_layer(Np, K, group_size=GROUP, density=DENSITY, r=RANK, seed=seed + 7919 * rank,
+                                 device=device)
+            elif world > 1:
+                Kp = K // world
+                L = S.make_layer(N, Kp, group_size=GROUP, group_offset=(rank * Kp) % GROUP, density=DENSITY,
+                                 r=RANK, seed=seed + 7919 * rank, device=device)
+            else:
+                L = S.make_layer(N, K, group_size=GROUP, density=DENSITY, r=RANK, seed=seed, device=device)
+            row[name] = L
+        layers.append(row)
+        torch.cuda.synchronize()
+    return layers
+
+
+def full_layer_bytes(M):
+    """Algorithmic bytes of one unsharded (linear, M) call of the recipe."""
+    tot = 0
+    for name, K, N in SHAPES:
+        wpr = ((K + 7) // 8 + 3) // 4 * 4
+        ng = (K + GROUP - 1) // GROUP
+        nnz = int(round(N * K * DENSITY))
+        ncsr = (K + 511) // 512
+        tot += N * wpr * 4 + N * ng * 32 + N * (ncsr + 1) * 4 + 3 * nnz
+        tot += N * RANK * 2 + N * 2 + M * RANK * 4 + M * K * 2 + M * N * 2
+    return tot
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from qwen_wlqfastshot_helen_beta_b200 import _C, _lib
+    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    peaks, peaks_kind = measured_peaks()
+    copies = args.copies
+    layers = build_layers(copies, rank, world, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+
+    # resident inputs per (copy, linear, M)
+    calls = []  # (copy, name, M, layer, x, h, out)
+    for c in range(copies):
+        for name, K, N in SHAPES:
+            L = layers[c][name]
+            for M in MS:
+                x = torch.randn((M, L.K), generator=gen, device=dev).to(torch.bfloat16)
+                h = S.lora_h(L, x)
+                out = torch.empty((M, L.N), dtype=torch.bfloat16, device=dev)
+                calls.append((c, name, M, L, x, h, out))
+    lib = _lib.lib
+    stream = torch.cuda.current_stream()
+
+    def launch(L, x, h, out):
+        rc = lib.wlq_gemm(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(L.q_packed.data_ptr()),
+                          ctypes.c_void_p(L.lut_c.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                          ctypes.c_void_p(L.chunk_offsets.data_ptr()), ctypes.c_void_p(L.chunk_cols.data_ptr()),
+                          ctypes.c_void_p(L.chunk_vals.data_ptr()), ctypes.c_void_p(h.data_ptr()),
+                          ctypes.c_void_p(L.lora_B.data_ptr()), ctypes.c_void_p(L.dora_gamma.data_ptr()),
+                          L.lora_scale, L.r, x.shape[0], L.N, L.K, 4, L.words_per_row, L.group_size,
+                          L.group_offset, _lib.WLQ_DTYPE_BF16, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        _lib.check(rc, "wlq_gemm")
+
+    def reduce_if_rowpar(name, out):
+        if world > 1 and name in ("o", "down"):
+            dist.all_reduce(out)
+
+    # one step per weight copy; per-kernel event nodes inside the graph
+    ge = GraphEvents()
+    per_copy = [[cl for cl in calls if cl[0] == c] for c in range(copies)]
+    steps_total = args.warmup + args.steps
+    order = [s % copies for s in range(steps_total)]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 16 * steps_total)]
+
+    # eager warm-up (also loads the kernels) before capture
+    for c in range(copies):
+        for (_, name, M, L, x, h, out) in per_copy[c]:
+            launch(L, x, h, out)
+            reduce_if_rowpar(name, out)
+    torch.cuda.synchronize()
+
+    def capture(step_range, ev_base):
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                e = ev_base
+                for st in step_range:
+                    for (_, name, M, L, x, h, out) in per_copy[order[st]]:
+                        ge.record(evs[e])
+                        launch(L, x, h, out)
+                        ge.record(evs[e + 1])
+                        e += 2
+                        reduce_if_rowpar(name, out)
+        torch.cuda.current_stream().wait_stream(s)
+        return g
+
+    g_warm = capture(range(0, args.warmup), 0)
+    g_time = capture(range(args.warmup, steps_total), 2 * 16 * args.warmup)
+    g_warm.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record()
+        g_time.replay()
+        t1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    kern_ms = 0.0
+    kern_bytes = 0
+    per_cfg = {}
+    e = 2 * 16 * args.warmup
+    for st in range(args.warmup, steps_total):
+        for (_, name, M, L, x, h, out) in per_copy[order[st]]:
+            d = evs[e].elapsed_time(evs[e + 1])  # kernel-only time of this launch
+            b = L.algorithmic_bytes(M)
+            kern_ms += d
+            kern_bytes += b
+            acc = per_cfg.setdefault(f"{name}/M{M}", [0.0, 0])
+            acc[0] += d
+            acc[1] += b
+            e += 2
+    step_bytes_rank = sum(cl[3].algorithmic_bytes(cl[2]) for cl in per_copy[0])
+    step_bytes_job = sum(full_layer_bytes(M) for M in MS) if world > 1 else step_bytes_rank
+    t = torch.tensor([elapsed_ms, kern_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, kern_ms_max = float(t[0]), float(t[1])
+    value = step_bytes_job * args.steps / (elapsed_ms * 1e-3) / 1e9
+
+    # ---- e2e: public op, host activations in, outputs out, every step
+    import qwen_wlqfastshot_helen_beta_b200  # noqa: F401  (torch ops)
+    host = []
+    for (c, name, M, L, x, h, out) in per_copy[0]:
+        xh = x.cpu().pin_memory()
+        hh = h.cpu().pin_memory()
+        oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        host.append((name, M, L, xh, hh, oh, torch.empty_like(x), torch.empty_like(h), torch.empty_like(out)))
+    h2d = sum(xh.numel() * xh.element_size() + hh.numel() * hh.element_size() for (_, _, _, xh, hh, *_r) in host)
+    d2h = sum(oh.numel() * oh.element_size() for (_, _, _, _, _, oh, *_r) in host)
+
+    def e2e_step():
+        for (name, M, L, xh, hh, oh, xd, hd, od) in host:
+            xd.copy_(xh, non_blocking=True)
+            hd.copy_(hh, non_blocking=True)
+            torch.ops.wlq_fastShot.gemm(xd, L.q_packed, L.lut_c, od, L.N, L.K, 4, L.words_per_row, L.chunk_offsets,
+                                        L.chunk_cols, L.chunk_vals, hd, L.lora_B, L.dora_gamma, L.lora_scale,
+                                        L.group_size, L.group_offset)
+            reduce_if_rowpar(name, od)
+            oh.copy_(od, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te[0])
+    e2e_value = step_bytes_job * args.steps / (e2e_ms * 1e-3) / 1e9
+
+    result = None
+    if rank == 0:
+        achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
+        peak = float(peaks["hbm_gbs"])
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+        if os.path.exists(tp):
+            with open(tp) as f:
+                traffic = json.load(f).get("bytes_per_step")
+        result = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(elapsed_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded; BASELINE config-1 recipe)",
+            "config": {
+                "workload": "qwen2.5-7b decode GEMV sweep (BASELINE config 1): qkv 3584->4608, o 3584->3584, "
+                            "gate_up 3584->37888, down 18944->3584 at M in {1,4,8,16}",
+                "group_size": GROUP, "lora_rank": RANK, "outlier_density": DENSITY, "act_dtype": "bf16",
+                "parallelism": f"tp{world}" if world > 1 else "single",
+                "l2": f"inputs larger than L2: {copies} rotating weight copies "
+                      f"({step_bytes_rank * copies / 1e6:.0f} MB per rank)",
+                "timing": "CUDA graph of K steps, events around the replay",
+            },
+            "roofline": {
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": f"{peaks_kind} hbm_gbs (MEASURED_PEAKS.json)" if peaks_kind == "measured"
+                else "fallback 6650 GB/s",
+                "kernel": "gemv_kernel (wlq_gemv.cu), all 16 (linear, M) launches of a step",
+                "per_config_gbs": {k: round(v[1] / (v[0] * 1e-3) / 1e9, 1) for k, v in per_cfg.items()},
+            },
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "path": "torch.ops.wlq_fastShot.gemm, pinned host buffers"},
+            "gpu_launches": 16 * args.steps,
+            "clocks": clk.summary(),
+        }
+    if world > 1:
+        del g_warm, g_time
+        dist.barrier()
+        dist.destroy_process_group()
+    return result, layers if rank == 0 else None
+
+
+# ---------------------------------------------------------- CPU baseline
+
+def _cpu_sample_layers(seed=5):
+    """Row blocks (<= 512 rows, full K) of each linear, generated on the CPU."""
+    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+    out = []
+    for si, (name, K, N) in enumerate(SHAPES):
+        rows = min(N, 512)
+        L = S.make_layer(rows, K, group_size=GROUP, density=DENSITY, r=RANK, seed=seed + si, device="cpu",
+                         row_block=128)
+        out.append((name, K, N, rows, L))
+    return out
+
+
+def _cpu_call(L, M, gen):
+    import torch
+    from oracle.cpu_baseline import cpu_forward
+    x = torch.randn((M, L.K), generator=gen).to(torch.bfloat16)
+    h = torch.nn.functional.linear(x.float(), L.lora_A.float())
+    t = time.perf_counter()
+    cpu_forward(L.q_packed.numpy(), L.words_per_row, L.lut_c, L.N, L.K, GROUP, 0, L.chunk_offsets.numpy(),
+                L.chunk_cols.numpy().astype(np.int64), L.chunk_vals.numpy(), x.float(), h, L.lora_B, L.dora_gamma,
+                L.lora_scale)
+    return time.perf_counter() - t, L.algorithmic_bytes(M)
+
+
+def cpu_baseline(budget_s=15.0):
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator()
+    gen.manual_seed(7)
+    layers = _cpu_sample_layers()
+    tot_t = tot_b = 0.0
+    n = 0
+    t_start = time.perf_counter()
+    _cpu_call(layers[0][4], 1, gen)  # warm-up
+    while True:
+        for (name, K, N, rows, L) in layers:
+            for M in MS:
+                dt, b = _cpu_call(L, M, gen)
+                tot_t += dt
+                tot_b += b
+                n += 1
+        if time.perf_counter() - t_start > budget_s:
+            break
+    return {"value": round(tot_b / tot_t / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{n} calls: 512-row blocks (full K) of each of the 4 linears at M in {{1,4,8,16}}, "
+                      f"the reference's torch dequantize-then-matmul steps (oracle/cpu_baseline.py), "
+                      f"{tot_t:.1f} s of CPU time"}
+
+
+def run_reference(args):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    gen = torch.Generator()
+    gen.manual_seed(11)
+    layers = _cpu_sample_layers()
+    cfgs = [(L, M) for (_, _, _, _, L) in layers for M in MS]
+    for s in range(args.warmup):
+        _cpu_call(*cfgs[s % len(cfgs)], gen)
+    tot_t = tot_b = 0.0
+    for s in range(args.steps):
+        dt, b = _cpu_call(*cfgs[s % len(cfgs)], gen)
+        tot_t += dt
+        tot_b += b
+    value = tot_b / tot_t / 1e9
+    cores = torch.get_num_threads()
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(tot_t * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE config-1 recipe)",
+        "config": {"workload": "qwen2.5-7b decode GEMV sweep (BASELINE config 1), CPU sample",
+                   "group_size": GROUP, "lora_rank": RANK, "outlier_density": DENSITY},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": "each step: one 512-row block (full K) of one linear at one M, cycling over "
+                                   "the 4 linears x M in {1,4,8,16}; the reference's torch dequantize-then-"
+                                   "matmul steps (oracle/cpu_baseline.py)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def run_case(args):
+    """One (linear, M) configuration, eager launches over `copies` rotating
+    weight copies: the small command the ncu captures profile."""
+    import torch
+    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+    name, M = args.case.split(":")
+    M = int(M)
+    K, N = {n: (k, nn) for n, k, nn in SHAPES}[name]
+    torch.cuda.set_device(0)
+    layers = [S.make_layer(N, K, group_size=GROUP, density=DENSITY, r=RANK, seed=300 + c) for c in range(args.copies)]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    x = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)
+    hs = [S.lora_h(L, x) for L in layers]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    for i in range(args.warmup):
+        S.forward(layers[i % len(layers)], x, out, hs[i % len(layers)])
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        S.forward(layers[i % len(layers)], x, out, hs[i % len(layers)])
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    b = layers[0].algorithmic_bytes(M)
+    print(json.dumps({"case": args.case, "ms_per_call": round(ms, 5), "bytes": b, "GB/s": round(b / ms / 1e6, 1)}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None, help="name:M, one configuration (profiling)")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--copies", type=int, default=3)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.case:
+        run_case(args)
+        return
+    if args.impl == "reference":
+        r = run_reference(args)
+        if r is not None:
+            print(json.dumps(r), flush=True)
+        return
+    result, _ = run_ours(args)
+    if result is not None:
+        world = result["n_gpus"]
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(args.cpu_budget)
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -159,7 +159,9 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvParams p) {
 #pragma unroll
         for (int j = 0; j < NT; ++j) load_x32<T>(x, 8 * j + g, p.M, p.K, kl, p.xvec, xa[j]);
         if (GROUPED) {
-            const int grp = (kl + p.goff) / p.G;
+            // lanes past K multiply zero activations; clamp their group so the
+            // codebook read stays inside the row
+            const int grp = min((kl + p.goff) / p.G, p.ngroups - 1);
             if (grp != cur_grp) {
                 cur_grp = grp;
                 load_planes<T>(p.lut, (int64_t)(v0 ? row0 : 0) * p.ngroups + grp, v0, P0);

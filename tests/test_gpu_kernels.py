@@ -1,0 +1,308 @@
+"""Parity of the sm_100a CUDA path with the oracle and with the reference's own
+CUDA kernels (compiled from source into oracle/_ref).  B200 only."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from _layers import make_np_layer, reference_output, rel_err
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+TOL = {torch.float16: 5e-3, torch.bfloat16: 2e-2}  # normwise max relative error
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    assert torch.cuda.is_available(), "the gpu tests need a CUDA device"
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+
+
+def C():
+    from qwen_wlqfastshot_helen_beta_b200 import _C
+    return _C
+
+
+def dev_layer(L):
+    d = "cuda"
+    t = {
+        "q": torch.from_numpy(L.q.view(np.int32)).to(d),
+        "lut": torch.from_numpy(np.ascontiguousarray(L.lut)).to(d),
+        "off": None if L.off is None else torch.from_numpy(L.off).to(d),
+        "cols": None if L.cols is None else torch.from_numpy(L.cols.astype(np.uint16)).to(d),
+        "vals": None if L.vals is None else torch.from_numpy(L.vals).to(d),
+        "A": None if L.A is None else torch.from_numpy(L.A).to(d),
+        "B": None if L.B is None else torch.from_numpy(L.B).to(d),
+        "gamma": None if L.gamma is None else torch.from_numpy(L.gamma).to(d),
+    }
+    return t
+
+
+def run_ours(L, T, x, h, gemv=False):
+    M = x.shape[0]
+    out = torch.full((M, L.N), float("nan"), dtype=x.dtype, device="cuda")
+    if gemv:
+        C().gemv_forward(T["q"], T["lut"], x, out, L.N, L.K, 4, T["off"], T["cols"], T["vals"], T["B"], h,
+                         T["gamma"], L.scale, L.G, L.goff)
+    else:
+        C().gemm_forward(x, T["q"], T["lut"], out, L.N, L.K, 4, L.wpr, T["off"], T["cols"], T["vals"], h, T["B"],
+                         T["gamma"], L.scale, L.G, L.goff)
+    torch.cuda.synchronize()
+    return out
+
+
+def inputs(rng, L, M, dtype):
+    x = torch.from_numpy(rng.standard_normal((M, L.K)).astype(np.float32)).to("cuda", dtype)
+    h = None
+    if L.A is not None:
+        h = torch.nn.functional.linear(x, torch.from_numpy(L.A).to("cuda", dtype)).float()
+    return x, h
+
+
+# ------------------------------------------------------------------ dequant
+
+@pytest.mark.parametrize("N,K,G,goff,density", [
+    (64, 1024, 0, 0, 0.01), (40, 203, 0, 0, 0.05), (33, 1100, 0, 0, 0.02), (7, 37, 0, 0, 0.3),
+    (48, 1000, 128, 0, 0.01), (20, 448, 128, 64, 0.02), (16, 640, 32, 0, 0.0), (5, 2, 0, 0, 0.5)])
+def test_dequant_bit_exact(N, K, G, goff, density):
+    rng = np.random.default_rng(N * 1000 + K)
+    L = make_np_layer(rng, N, K, G, goff, density=density, outliers=density > 0)
+    T = dev_layer(L)
+    W = torch.empty((N, K), dtype=torch.float16, device="cuda")
+    C().dequant_w0(T["q"], T["lut"], W, N, K, 4, L.wpr, T["off"], T["cols"], T["vals"], G, goff)
+    torch.cuda.synchronize()
+    assert np.array_equal(W.cpu().numpy().view(np.uint16), L.dense().view(np.uint16))
+
+
+def test_dequant_other_bit_widths():
+    rng = np.random.default_rng(9)
+    for bits, (N, K) in [(1, (9, 70)), (2, (5, 33)), (3, (6, 1300))]:
+        idx = rng.integers(0, 1 << bits, size=(N, K), dtype=np.uint8)
+        q, wpr = O.pack_row_aligned(idx, bits)
+        lut = rng.standard_normal((N, 1 << bits)).astype(np.float16)
+        chunk_m = 640 if bits == 3 else 512
+        off, cols = O.build_chunk_csr(rng.random((N, K)) < 0.05, chunk_m)
+        vals = rng.integers(0, 256, size=cols.size, dtype=np.uint8)
+        ref = O.dequant(q, wpr, lut, N, K, bits, 0, 0, off, cols, vals, chunk_m)
+        W = torch.empty((N, K), dtype=torch.float16, device="cuda")
+        C().dequant_w0(torch.from_numpy(q.view(np.int32)).cuda(), torch.from_numpy(lut).cuda(), W, N, K, bits, wpr,
+                       torch.from_numpy(off).cuda(), torch.from_numpy(cols).cuda(), torch.from_numpy(vals).cuda())
+        torch.cuda.synchronize()
+        assert np.array_equal(W.cpu().numpy().view(np.uint16), ref.view(np.uint16)), bits
+
+
+# --------------------------------------------------------- GEMV vs oracle
+
+LAYER_CASES = [
+    # N, K, G, goff, outliers, dora
+    (64, 1024, 0, 0, True, True),
+    (40, 203, 0, 0, True, True),       # ragged K, N not a multiple of 16
+    (100, 4096, 128, 0, True, True),   # per-group codebooks
+    (48, 448, 128, 64, True, False),   # tensor-parallel shard starting mid-group
+    (33, 1100, 32, 0, False, True),
+    (16, 130, 0, 0, True, False),
+]
+
+
+@pytest.mark.parametrize("case", LAYER_CASES, ids=lambda c: f"N{c[0]}K{c[1]}G{c[2]}o{c[3]}")
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_gemv_matches_oracle(case, dtype):
+    N, K, G, goff, outl, dora = case
+    rng = np.random.default_rng(N + K + G)
+    L = make_np_layer(rng, N, K, G, goff, density=0.02, outliers=outl, dora=dora)
+    T = dev_layer(L)
+    for M in (1, 2, 3, 7, 8, 9, 15, 16):
+        x, h = inputs(rng, L, M, dtype)
+        y = run_ours(L, T, x, h, gemv=(M == 1))
+        ref = reference_output(L, x.float().cpu().numpy(), None if h is None else h.cpu().numpy())
+        e = rel_err(y.float().cpu().numpy(), ref)
+        assert e <= TOL[dtype], (M, e)
+        assert torch.isfinite(y).all()
+
+
+def test_gemv_outlier_edges():
+    """Outliers at the first and last column, in a ragged last chunk, a row
+    made only of outliers, and rows without any."""
+    rng = np.random.default_rng(77)
+    N, K = 24, 1100
+    L = make_np_layer(rng, N, K, 0, 0, outliers=False, dora=True)
+    mask = np.zeros((N, K), bool)
+    mask[0, 0] = mask[0, K - 1] = True
+    mask[1, 1024:] = True
+    mask[2, :] = True
+    mask[5, 511:513] = True
+    L.off, L.cols = O.build_chunk_csr(mask, 512)
+    L.vals = O.fp16_to_fp8_bytes((rng.standard_normal(L.cols.size) * 0.1).astype(np.float16))
+    T = dev_layer(L)
+    for M in (1, 4, 16):
+        for dtype in (torch.float16, torch.bfloat16):
+            x, h = inputs(rng, L, M, dtype)
+            y = run_ours(L, T, x, h)
+            ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+            assert rel_err(y.float().cpu().numpy(), ref) <= TOL[dtype], (M, dtype)
+
+
+# ------------------------------------------------- the reference's kernels
+
+def _ref_lib():
+    path = os.path.join(ROOT, "oracle", "_ref", "libwlq_ref_kernels.so")
+    if not os.path.exists(path):
+        pytest.skip("reference kernels not built (oracle/build_ref.sh needs the reference tree)")
+    lib = ctypes.CDLL(path)
+    return lib
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+@pytest.mark.parametrize("N,K", [(256, 1024), (96, 3584), (40, 512)])
+def test_against_reference_kernels(N, K):
+    """Same inputs through launch_gemv_chunk_csr (M=1), launch_gemm_metalog_dora
+    (2<=M<=15) and dequant + cuBLAS + epilogue (M>=16), the reference's three
+    paths (csrc/vllm_binding.cpp:253-419); fp16, per-row codebooks."""
+    lib = _ref_lib()
+    rng = np.random.default_rng(N * K)
+    L = make_np_layer(rng, N, K, 0, 0, density=0.01, outliers=True, dora=True)
+    T = dev_layer(L)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    nc = (K + 511) // 512
+    i, f = ctypes.c_int, ctypes.c_float
+    # bit-exact dequant against launch_dequant_patch_metalog
+    Wr = torch.empty((N, K), dtype=torch.float16, device="cuda")
+    lib.launch_dequant_patch_metalog(_p(T["q"]), _p(T["lut"]), _p(Wr), _p(T["off"]), _p(T["cols"]), _p(T["vals"]),
+                                     i(N), i(K), i(4), i(L.wpr), i(nc), i(512), stream)
+    Wm = torch.empty_like(Wr)
+    C().dequant_w0(T["q"], T["lut"], Wm, N, K, 4, L.wpr, T["off"], T["cols"], T["vals"])
+    torch.cuda.synchronize()
+    assert torch.equal(Wr.view(torch.int16), Wm.view(torch.int16))
+    ws = torch.zeros(32 * N, dtype=torch.float32, device="cuda")
+    for M in (1, 4, 15, 16, 32):
+        x, h = inputs(rng, L, M, torch.float16)
+        ref = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        if M == 1:
+            lib.launch_gemv_chunk_csr(_p(T["q"]), _p(T["lut"]), _p(x), _p(ref), _p(ws), _p(T["off"]), _p(T["cols"]),
+                                      _p(T["vals"]), _p(T["B"]), _p(h), _p(T["gamma"]), f(L.scale), i(L.r), i(N),
+                                      i(K), i(4), i(nc), stream)
+        elif M < 16:
+            lib.launch_gemm_metalog_dora(_p(x), _p(T["q"]), _p(T["lut"]), _p(ref), _p(T["off"]), _p(T["cols"]),
+                                         _p(T["vals"]), _p(h), _p(T["B"]), _p(T["gamma"]), f(L.scale), i(L.r), i(M),
+                                         i(N), i(K), i(4), i(L.wpr), i(nc), i(512), stream)
+        else:
+            torch.mm(x, Wr.t(), out=ref)
+            lib.launch_fused_dora_epilogue(_p(ref), _p(h), _p(T["B"]), _p(T["gamma"]), f(L.scale), i(L.r), i(M), i(N),
+                                           stream)
+        torch.cuda.synchronize()
+        if M > 16:
+            continue  # no tcgen05 GEMM comparison until that path exists in this build
+        y = run_ours(L, T, x, h, gemv=(M == 1))
+        oracle = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+        e_ours = rel_err(y.float().cpu().numpy(), oracle)
+        e_ref = rel_err(ref.float().cpu().numpy(), oracle)
+        e_pair = rel_err(y.float().cpu().numpy(), ref.float().cpu().numpy())
+        assert e_ours <= 5e-3 and e_ref <= 5e-3 and e_pair <= 5e-3, (M, e_ours, e_ref, e_pair)
+
+
+# ------------------------------------------------------------- full sizes
+
+@pytest.mark.parametrize("name", ["qkv", "o", "gate_up", "down"])
+def test_full_size_shapes(name):
+    """BASELINE config-1 shapes with the benchmark recipe (128-wide codebook
+    groups, rank 16, 0.5% outliers): dequantisation spot-checked bit-exact
+    against the oracle on sampled rows, and the GEMV against the dequantised
+    weights times x in fp32 on the GPU."""
+    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+    K, N = S.QWEN25_7B[name]
+    L = S.make_layer(N, K, group_size=128, density=0.005, r=16, seed=11)
+    W = torch.empty((N, K), dtype=torch.float16, device="cuda")
+    C().dequant_w0(L.q_packed, L.lut_c, W, N, K, 4, L.words_per_row, L.chunk_offsets, L.chunk_cols, L.chunk_vals,
+                   128, 0)
+    rows = np.random.default_rng(1).choice(N, size=16, replace=False)
+    q = L.q_packed.view(N, L.words_per_row).cpu().numpy()
+    lut = L.lut_c.cpu().numpy()
+    off = L.chunk_offsets.cpu().numpy()
+    cols = L.chunk_cols.cpu().numpy()
+    vals = L.chunk_vals.cpu().numpy()
+    for r in rows:
+        a, b = off[r, 0], off[r, -1]
+        ref = O.dequant(q[r], L.words_per_row, lut[r:r + 1], 1, K, 4, 128, 0, off[r:r + 1] - a, cols[a:b], vals[a:b])
+        assert np.array_equal(W[r].cpu().numpy().view(np.uint16), ref[0].view(np.uint16)), r
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    Wf = W.float()
+    for M in (1, 16):
+        x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+        h = S.lora_h(L, x)
+        y = S.forward(L, x, h=h)
+        ref = (x.float() @ Wf.t() + L.lora_scale * (h @ L.lora_B.float().t())) * L.dora_gamma.float()
+        # the kernel multiplies bf16-rounded codebook values; compare against both
+        e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
+        assert e <= 2e-2, (name, M, e)
+    del W, Wf
+
+
+# ------------------------------------------------------ torch op surface
+
+def test_custom_ops_opcheck_and_graph_capture():
+    import qwen_wlqfastshot_helen_beta_b200  # noqa: F401  (registers the ops)
+    rng = np.random.default_rng(4)
+    L = make_np_layer(rng, 128, 512, 0, 0, density=0.01)
+    T = dev_layer(L)
+    x, h = inputs(rng, L, 1, torch.float16)
+    out = torch.empty((1, L.N), dtype=torch.float16, device="cuda")
+    args = (T["q"], T["lut"], x.squeeze(0), out.squeeze(0), L.N, L.K, 4, T["off"], T["cols"], T["vals"], T["B"],
+            h.squeeze(0), T["gamma"], L.scale)
+    torch.library.opcheck(torch.ops.wlq_fastShot.gemv.default, args)
+    X, H = inputs(rng, L, 8, torch.float16)
+    out8 = torch.empty((8, L.N), dtype=torch.float16, device="cuda")
+    gargs = (X, T["q"], T["lut"], out8, L.N, L.K, 4, L.wpr, T["off"], T["cols"], T["vals"], H, T["B"], T["gamma"],
+             L.scale)
+    torch.library.opcheck(torch.ops.wlq_fastShot.gemm.default, gargs)
+    # capture both ops in one CUDA graph and replay with new inputs
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            torch.ops.wlq_fastShot.gemv(*args)
+            torch.ops.wlq_fastShot.gemm(*gargs)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        torch.ops.wlq_fastShot.gemv(*args)
+        torch.ops.wlq_fastShot.gemm(*gargs)
+    x2, h2 = inputs(rng, L, 1, torch.float16)
+    X2, H2 = inputs(rng, L, 8, torch.float16)
+    x.copy_(x2)
+    h.copy_(h2)
+    X.copy_(X2)
+    H.copy_(H2)
+    graph.replay()
+    torch.cuda.synchronize()
+    e1 = run_ours(L, T, x, h, gemv=True)
+    e8 = run_ours(L, T, X, H)
+    assert torch.equal(out, e1) and torch.equal(out8, e8)
+
+
+def test_errors_are_raised():
+    rng = np.random.default_rng(2)
+    L = make_np_layer(rng, 32, 256, 0, 0)
+    T = dev_layer(L)
+    x, h = inputs(rng, L, 2, torch.float16)
+    out = torch.empty((2, 32), dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError, match="4-bit"):
+        C().gemm_forward(x, T["q"], T["lut"], out, 32, 256, 3, 28, None, None, None)
+    with pytest.raises(RuntimeError, match="dtype"):
+        C().gemm_forward(x, T["q"], T["lut"], out.to(torch.bfloat16), 32, 256, 4, L.wpr, None, None, None)
+    with pytest.raises(RuntimeError, match="float16 or bfloat16"):
+        C().gemm_forward(x.float(), T["q"], T["lut"], out.float(), 32, 256, 4, L.wpr, None, None, None)
+    with pytest.raises(RuntimeError, match="lut_c"):
+        C().gemm_forward(x, T["q"], T["lut"][:16], out, 32, 256, 4, L.wpr, None, None, None)
+    with pytest.raises(RuntimeError, match="multiples of 32"):
+        C().gemm_forward(x, T["q"], torch.zeros(32 * 3 * 16, dtype=torch.float16, device="cuda"), out, 32, 256, 4,
+                         L.wpr, None, None, None, lut_group_size=128, lut_group_offset=16)
