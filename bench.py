@@ -167,7 +167,7 @@ def build_layers(copies, rank, world, device, seed0=1000):
                                  r=RANK, seed=seed + 7919 * rank, device=device)
             else:
                 L = S.make_layer(N, K, group_size=GROUP, density=DENSITY, r=RANK, seed=seed, device=device)
-            row[name] = L
+            row[name] = L.prepack(torch.bfloat16)
         layers.append(row)
         torch.cuda.synchronize()
     return layers
@@ -221,12 +221,13 @@ def run_ours(args):
 
     def launch(L, x, h, out):
         rc = lib.wlq_gemm(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(L.q_packed.data_ptr()),
-                          ctypes.c_void_p(L.lut_c.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-                          ctypes.c_void_p(L.chunk_offsets.data_ptr()), ctypes.c_void_p(L.chunk_cols.data_ptr()),
-                          ctypes.c_void_p(L.chunk_vals.data_ptr()), ctypes.c_void_p(h.data_ptr()),
+                          ctypes.c_void_p(L.lut_packed.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                          ctypes.c_void_p(L.chunk_offsets.data_ptr()), ctypes.c_void_p(L.cols_packed.data_ptr()),
+                          ctypes.c_void_p(L.delta_packed.data_ptr()), ctypes.c_void_p(h.data_ptr()),
                           ctypes.c_void_p(L.lora_B.data_ptr()), ctypes.c_void_p(L.dora_gamma.data_ptr()),
                           L.lora_scale, L.r, x.shape[0], L.N, L.K, 4, L.words_per_row, L.group_size,
-                          L.group_offset, _lib.WLQ_DTYPE_BF16, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+                          L.group_offset, _lib.WLQ_LUT_PREPACKED, _lib.WLQ_DTYPE_BF16,
+                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         _lib.check(rc, "wlq_gemm")
 
     def reduce_if_rowpar(name, out):
@@ -239,6 +240,8 @@ def run_ours(args):
     steps_total = args.warmup + args.steps
     order = [s % copies for s in range(steps_total)]
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 16 * steps_total)]
+    for ev in evs:  # torch creates the CUDA event on first record; do it outside capture
+        ev.record()
 
     # eager warm-up (also loads the kernels) before capture
     for c in range(copies):
@@ -317,9 +320,9 @@ def run_ours(args):
         for (name, M, L, xh, hh, oh, xd, hd, od) in host:
             xd.copy_(xh, non_blocking=True)
             hd.copy_(hh, non_blocking=True)
-            torch.ops.wlq_fastShot.gemm(xd, L.q_packed, L.lut_c, od, L.N, L.K, 4, L.words_per_row, L.chunk_offsets,
-                                        L.chunk_cols, L.chunk_vals, hd, L.lora_B, L.dora_gamma, L.lora_scale,
-                                        L.group_size, L.group_offset)
+            torch.ops.wlq_fastShot.gemm(xd, L.q_packed, L.lut_packed, od, L.N, L.K, 4, L.words_per_row,
+                                        L.chunk_offsets, L.cols_packed, L.delta_packed, hd, L.lora_B, L.dora_gamma,
+                                        L.lora_scale, L.group_size, L.group_offset, 1)
             reduce_if_rowpar(name, od)
             oh.copy_(od, non_blocking=True)
         torch.cuda.current_stream().synchronize()
@@ -486,7 +489,8 @@ def run_case(args):
     M = int(M)
     K, N = {n: (k, nn) for n, k, nn in SHAPES}[name]
     torch.cuda.set_device(0)
-    layers = [S.make_layer(N, K, group_size=GROUP, density=DENSITY, r=RANK, seed=300 + c) for c in range(args.copies)]
+    layers = [S.make_layer(N, K, group_size=GROUP, density=DENSITY, r=RANK, seed=300 + c).prepack(torch.bfloat16)
+              for c in range(args.copies)]
     gen = torch.Generator(device="cuda")
     gen.manual_seed(5)
     x = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)

@@ -60,6 +60,17 @@ enum wlq_status {
 
 enum wlq_dtype { WLQ_DTYPE_F16 = 0, WLQ_DTYPE_BF16 = 1 };
 
+/* Layout of the codebooks and outliers given to wlq_gemv / wlq_gemm.
+ * WLQ_LUT_F16: the reference's layout (16 fp16 entries per codebook; outliers
+ * as chunk-local columns and e5m2 bytes).
+ * WLQ_LUT_PREPACKED: the load-time layout for one act_dtype, made once by
+ * wlq_prepack_lut (codebooks: entries rounded to the MMA type, bytes split
+ * into planes; same size and indexing) and wlq_prepack_outliers (chunk_cols
+ * then holds uint16 global columns and chunk_vals points to float32
+ * corrections w_outlier - codebook value; chunk_offsets unchanged), so the
+ * kernels never convert codebooks or look up outlier codebook values. */
+enum wlq_lut_format { WLQ_LUT_F16 = 0, WLQ_LUT_PREPACKED = 1 };
+
 /* Message of the last failed call on this thread ("" if none). */
 WLQ_API const char* wlq_last_error(void);
 /* ABI revision of this header. */
@@ -76,7 +87,7 @@ WLQ_API int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, 
              const int32_t* chunk_offsets, const uint16_t* chunk_cols, const uint8_t* chunk_vals,
              const void* lora_B, const float* lora_h, const void* dora_gamma, float lora_scale,
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
-             int lut_group_offset, int act_dtype, wlq_stream_t stream);
+             int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
 
 /* Batched forward for any M >= 1: M <= 16 runs the GEMV-class kernel, larger
  * M the tcgen05 tensor-core GEMM with dequantisation, outlier replacement and
@@ -87,7 +98,25 @@ WLQ_API int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, 
              const int32_t* chunk_offsets, const uint16_t* chunk_cols, const uint8_t* chunk_vals,
              const float* lora_H, const void* lora_B, const void* dora_gamma, float lora_scale,
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
-             int lut_group_offset, int act_dtype, wlq_stream_t stream);
+             int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
+
+/* Codebooks -> WLQ_LUT_PREPACKED layout for act_dtype: n_codebooks x 16 fp16
+ * entries in, the same number of 32-byte records out (may not alias).  Done
+ * once at load time; no reference counterpart (the reference converts per
+ * call inside its kernels). */
+WLQ_API int wlq_prepack_lut(const void* lut_c, void* lut_out, int64_t n_codebooks, int act_dtype,
+                            wlq_stream_t stream);
+
+/* Outliers -> the WLQ_LUT_PREPACKED outlier stream for act_dtype: per chunk-CSR
+ * entry, in the same order, the global column (uint16, K <= 65535; 0xFFFF for
+ * an entry past K) and the float32 correction w_outlier - codebook value with
+ * the codebook entry rounded to the MMA type.  Inputs are in the reference
+ * layout (fp16 codebooks).  No reference counterpart (the reference re-reads
+ * the index word and codebook per outlier, csrc/gemv_kernel.cu:262-288). */
+WLQ_API int wlq_prepack_outliers(const int32_t* q_packed, const void* lut_c, const int32_t* chunk_offsets,
+                                 const uint16_t* chunk_cols, const uint8_t* chunk_vals, int64_t nnz, int N,
+                                 int K, int bits, int words_per_row, int lut_group_size, int lut_group_offset,
+                                 int act_dtype, uint16_t* cols_out, float* delta_out, wlq_stream_t stream);
 
 /* Dense fp16 W[N, K] (codebook gather, then outliers overwritten), bit-exact
  * with the reference.  bits 1..4.  Replaces launch_dequant_patch_metalog
@@ -149,6 +178,9 @@ WLQ_API int wlq_build_chunk_csr(const uint8_t* mask, int64_t N, int64_t K, int64
 /* fp16 outlier values -> e5m2 bytes, (u16 + 0x80) >> 8 clamped
  * (vllm_wlq/linear_method.py:306-308, 519-521). */
 WLQ_API int wlq_fp16_to_fp8_bytes(const uint16_t* src, int64_t n, uint8_t* dst);
+
+/* Host twin of wlq_prepack_lut. */
+WLQ_API int wlq_prepack_lut_host(const uint16_t* lut_c, uint16_t* lut_out, int64_t n_codebooks, int act_dtype);
 
 /* Host twin of wlq_dequant, for loading without a GPU (the reference's
  * gather fallback, vllm_wlq/linear_method.py:608-623). */

@@ -19,7 +19,7 @@ from typing import Optional, Tuple
 import numpy as np
 import torch
 
-from ._lib import WLQ_DTYPE_BF16, WLQ_DTYPE_F16, check, lib
+from ._lib import WLQ_DTYPE_BF16, WLQ_DTYPE_F16, WLQ_LUT_F16, WLQ_LUT_PREPACKED, check, lib
 
 _NONE = None
 
@@ -68,8 +68,9 @@ def _check_opt(name, nm, t, dtype, device):
 
 
 def _linear_checks(name, x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lora_B, lora_h, gamma,
-                   group_size, group_offset):
+                   group_size, group_offset, lut_format=WLQ_LUT_F16):
     _check_common(name, (q_packed, lut_c, x, out), ("q_packed", "lut_c", "x", "out"))
+    _require(bits == 4, f"{name}: the fused kernels read 4-bit indices only (bits={bits})")
     dev = x.device
     for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("out", out)):
         _require(t.device == dev, f"{name}: {nm} must be on {dev}")
@@ -89,7 +90,8 @@ def _linear_checks(name, x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, v
         nc = (K + chunk_m - 1) // chunk_m
         _check_opt(name, "chunk_offsets", offs, torch.int32, dev)
         _check_opt(name, "chunk_cols", cols, torch.uint16, dev)
-        _check_opt(name, "chunk_vals", vals, torch.uint8, dev)
+        # prepacked layers carry float32 corrections in place of e5m2 bytes
+        _check_opt(name, "chunk_vals", vals, torch.float32 if lut_format == WLQ_LUT_PREPACKED else torch.uint8, dev)
         _require(offs.numel() == N * (nc + 1), f"{name}: chunk_offsets must be [{N}, {nc + 1}]")
         _require(cols.numel() == vals.numel(), f"{name}: chunk_cols and chunk_vals lengths differ")
     r = 0
@@ -131,34 +133,36 @@ class _DeviceGuard:
 
 def gemv_forward(q_packed, lut_c, x, out, N, K, bits, chunk_offsets=None, chunk_cols=None, chunk_vals=None,
                  lora_B=None, lora_h=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
-                 lut_group_offset=0):
+                 lut_group_offset=0, lut_format=WLQ_LUT_F16):
     """Decode GEMV, M = x.numel() / K <= 16 (csrc/vllm_binding.cpp:253-315)."""
     N, K, bits = int(N), int(K), int(bits)
     offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
     lb, lh, gm = _opt(lora_B), _opt(lora_h), _opt(dora_gamma)
     wpr = words_per_row(K, bits)
     M, r = _linear_checks("gemv_forward", x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lb, lh, gm,
-                          int(lut_group_size), int(lut_group_offset))
+                          int(lut_group_size), int(lut_group_offset), int(lut_format))
     with _DeviceGuard(x.device):
         rc = lib.wlq_gemv(_ptr(q_packed), _ptr(lut_c), _ptr(x), _ptr(out), _ptr(offs), _ptr(cols), _ptr(vals),
                           _ptr(lb), _ptr(lh), _ptr(gm), float(lora_scale), r, M, N, K, bits, wpr,
-                          int(lut_group_size), int(lut_group_offset), _act_dtype(x), _stream(x.device))
+                          int(lut_group_size), int(lut_group_offset), int(lut_format), _act_dtype(x),
+                          _stream(x.device))
     check(rc, "wlq_gemv")
 
 
 def gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,
                  chunk_vals=None, lora_H=None, lora_B=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
-                 lut_group_offset=0):
+                 lut_group_offset=0, lut_format=WLQ_LUT_F16):
     """Batched forward for any M (csrc/vllm_binding.cpp:318-419)."""
     N, K, bits, wpr = int(N), int(K), int(bits), int(words_per_row)
     offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
     lb, lh, gm = _opt(lora_B), _opt(lora_H), _opt(dora_gamma)
     M, r = _linear_checks("gemm_forward", X, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lb, lh, gm,
-                          int(lut_group_size), int(lut_group_offset))
+                          int(lut_group_size), int(lut_group_offset), int(lut_format))
     with _DeviceGuard(X.device):
         rc = lib.wlq_gemm(_ptr(X), _ptr(q_packed), _ptr(lut_c), _ptr(out), _ptr(offs), _ptr(cols), _ptr(vals),
                           _ptr(lh), _ptr(lb), _ptr(gm), float(lora_scale), r, M, N, K, bits, wpr,
-                          int(lut_group_size), int(lut_group_offset), _act_dtype(X), _stream(X.device))
+                          int(lut_group_size), int(lut_group_offset), int(lut_format), _act_dtype(X),
+                          _stream(X.device))
     check(rc, "wlq_gemm")
 
 
@@ -190,6 +194,46 @@ def dequant_w0(q_packed, lut_c, W_out, N, K, bits, words_per_row, chunk_offsets,
     rc = lib.wlq_dequant_host(_ptr(q_packed), _ptr(lut_c), _ptr(W_out), _ptr(offs), _ptr(cols), _ptr(vals),
                               N, K, bits, wpr, int(lut_group_size), int(lut_group_offset))
     check(rc, "wlq_dequant_host")
+
+
+def prepack_lut(lut_c: torch.Tensor, act_dtype: torch.dtype) -> torch.Tensor:
+    """fp16 codebooks (any shape ending in 16) -> the WLQ_LUT_PREPACKED layout
+    for `act_dtype` (same shape, stored as float16 bits).  CUDA tensors use the
+    GPU kernel, CPU tensors the host codec."""
+    _require(lut_c.dtype == torch.float16 and lut_c.is_contiguous() and lut_c.shape[-1] == 16,
+             "prepack_lut: lut_c must be a contiguous float16 tensor with 16 entries per codebook")
+    dt = WLQ_DTYPE_BF16 if act_dtype == torch.bfloat16 else WLQ_DTYPE_F16
+    out = torch.empty_like(lut_c)
+    n = lut_c.numel() // 16
+    if lut_c.is_cuda:
+        with _DeviceGuard(lut_c.device):
+            check(lib.wlq_prepack_lut(_ptr(lut_c), _ptr(out), n, dt, _stream(lut_c.device)), "wlq_prepack_lut")
+    else:
+        check(lib.wlq_prepack_lut_host(_ptr(lut_c), _ptr(out), n, dt), "wlq_prepack_lut_host")
+    return out
+
+
+def prepack_outliers(q_packed, lut_c, chunk_offsets, chunk_cols, chunk_vals, N, K, bits, act_dtype,
+                     lut_group_size=0, lut_group_offset=0):
+    """Reference-layout outliers -> (uint16 global columns, float32 corrections)
+    for `act_dtype`, the WLQ_LUT_PREPACKED outlier stream (CUDA tensors)."""
+    offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
+    if offs is None or cols is None or vals is None:
+        return None, None
+    dev = q_packed.device
+    for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("chunk_offsets", offs), ("chunk_cols", cols),
+                  ("chunk_vals", vals)):
+        _require(t.is_cuda and t.device == dev and t.is_contiguous(), f"prepack_outliers: {nm} must be on {dev}")
+    _require(vals.dtype == torch.uint8 and cols.dtype == torch.uint16, "prepack_outliers: e5m2 bytes / uint16 cols")
+    gcols = torch.empty_like(cols)
+    delta = torch.empty(cols.numel(), dtype=torch.float32, device=dev)
+    dt = WLQ_DTYPE_BF16 if act_dtype == torch.bfloat16 else WLQ_DTYPE_F16
+    with _DeviceGuard(dev):
+        rc = lib.wlq_prepack_outliers(_ptr(q_packed), _ptr(lut_c), _ptr(offs), _ptr(cols), _ptr(vals), cols.numel(),
+                                      int(N), int(K), int(bits), words_per_row(K, bits), int(lut_group_size),
+                                      int(lut_group_offset), dt, _ptr(gcols), _ptr(delta), _stream(dev))
+    check(rc, "wlq_prepack_outliers")
+    return gcols, delta
 
 
 def init_workspaces(max_N, max_K, device):

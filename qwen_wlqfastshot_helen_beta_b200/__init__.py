@@ -37,14 +37,15 @@ def _register_ops():
         lora_scale: float = 1.0,
         lut_group_size: int = 0,
         lut_group_offset: int = 0,
+        lut_format: int = 0,
     ) -> None:
         _C.gemv_forward(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
-                        lora_h, dora_gamma, lora_scale, lut_group_size, lut_group_offset)
+                        lora_h, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
 
     @_gemv_op.register_fake
     def _gemv_fake(q_packed, lut_c, x, out, N, K, bits, chunk_offsets=None, chunk_cols=None, chunk_vals=None,
                    lora_B=None, lora_h=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
-                   lut_group_offset=0):
+                   lut_group_offset=0, lut_format=0):
         return None
 
     @torch.library.custom_op("wlq_fastShot::gemm", mutates_args={"out"})
@@ -66,14 +67,16 @@ def _register_ops():
         lora_scale: float = 1.0,
         lut_group_size: int = 0,
         lut_group_offset: int = 0,
+        lut_format: int = 0,
     ) -> None:
         _C.gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets, chunk_cols,
-                        chunk_vals, lora_H, lora_B, dora_gamma, lora_scale, lut_group_size, lut_group_offset)
+                        chunk_vals, lora_H, lora_B, dora_gamma, lora_scale, lut_group_size, lut_group_offset,
+                        lut_format)
 
     @_gemm_op.register_fake
     def _gemm_fake(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,
                    chunk_vals=None, lora_H=None, lora_B=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
-                   lut_group_offset=0):
+                   lut_group_offset=0, lut_format=0):
         return None
 
 

@@ -14,6 +14,8 @@ LIB_PATH = os.path.join(_HERE, "libwlq_b200.so")
 WLQ_OK = 0
 WLQ_DTYPE_F16 = 0
 WLQ_DTYPE_BF16 = 1
+WLQ_LUT_F16 = 0
+WLQ_LUT_PREPACKED = 1
 ABI_VERSION = 1
 
 _i32, _i64, _f32, _p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
@@ -24,9 +26,13 @@ SIGNATURES = {
     "wlq_last_error": (ctypes.c_char_p, []),
     "wlq_abi_version": (_i32, []),
     "wlq_gemv": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
-                        _i32, _i32, _i32, _p]),
+                        _i32, _i32, _i32, _i32, _p]),
     "wlq_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
-                        _i32, _i32, _i32, _p]),
+                        _i32, _i32, _i32, _i32, _p]),
+    "wlq_prepack_lut": (_i32, [_p, _p, _i64, _i32, _p]),
+    "wlq_prepack_lut_host": (_i32, [_p, _p, _i64, _i32]),
+    "wlq_prepack_outliers": (_i32, [_p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p,
+                                    _p]),
     "wlq_dequant": (_i32, [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p]),
     "wlq_init_workspaces": (_i32, [_i64, _i64, _i32]),
     "wlq_words_per_row": (_i64, [_i64, _i32]),

@@ -61,12 +61,15 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 int build_args(const char* fn, const void* x, const int32_t* q, const void* lut, void* out,
                const int32_t* off, const uint16_t* ccols, const uint8_t* cvals, const void* loraB,
                const float* lorah, const void* gamma, float scale, int r, int M, int N, int K, int bits,
-               int wpr, int G, int goff, int dtype, LinearArgs& a) {
+               int wpr, int G, int goff, int lut_format, int dtype, LinearArgs& a) {
     if (M < 0 || N < 0 || K < 0) return fail(WLQ_ERR_INVALID_ARG, "%s: negative size (M=%d N=%d K=%d)", fn, M, N, K);
     if (bits != 4)
         return fail(WLQ_ERR_UNSUPPORTED, "%s: only 4-bit indices are supported by the fused kernels (bits=%d)", fn, bits);
     if (dtype != WLQ_DTYPE_F16 && dtype != WLQ_DTYPE_BF16)
         return fail(WLQ_ERR_UNSUPPORTED, "%s: act_dtype must be WLQ_DTYPE_F16 or WLQ_DTYPE_BF16 (got %d)", fn, dtype);
+    if (lut_format != WLQ_LUT_F16 && lut_format != WLQ_LUT_PREPACKED)
+        return fail(WLQ_ERR_INVALID_ARG, "%s: lut_format must be WLQ_LUT_F16 or WLQ_LUT_PREPACKED (got %d)", fn,
+                    lut_format);
     if (M > 0 && N > 0 && K > 0 && (!x || !q || !lut || !out))
         return fail(WLQ_ERR_INVALID_ARG, "%s: x, q_packed, lut_c and out are required", fn);
     const int64_t need_wpr = words_per_row(K, bits);
@@ -102,6 +105,7 @@ int build_args(const char* fn, const void* x, const int32_t* q, const void* lut,
     a.chunk_m = chunk_m_for_bits(bits);
     a.ncsr = (K + a.chunk_m - 1) / a.chunk_m;
     a.dtype = dtype;
+    a.lut_prepacked = lut_format == WLQ_LUT_PREPACKED;
     return WLQ_OK;
 }
 }  // namespace
@@ -125,12 +129,12 @@ int wlq_abi_version(void) { return WLQ_ABI_VERSION; }
 int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, void* out, const int32_t* chunk_offsets,
              const uint16_t* chunk_cols, const uint8_t* chunk_vals, const void* lora_B, const float* lora_h,
              const void* dora_gamma, float lora_scale, int r, int M, int N, int K, int bits, int words_per_row,
-             int lut_group_size, int lut_group_offset, int act_dtype, wlq_stream_t stream) {
+             int lut_group_size, int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream) {
     g_last_error[0] = '\0';
     LinearArgs a;
     int rc = build_args("wlq_gemv", x, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_h,
                         dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size, lut_group_offset,
-                        act_dtype, a);
+                        lut_format, act_dtype, a);
     if (rc) return rc;
     if (M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: M must be 1..16 (got %d); use wlq_gemm", M);
     if (M == 0 || N == 0) return WLQ_OK;
@@ -141,12 +145,12 @@ int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, void* ou
 int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* out, const int32_t* chunk_offsets,
              const uint16_t* chunk_cols, const uint8_t* chunk_vals, const float* lora_H, const void* lora_B,
              const void* dora_gamma, float lora_scale, int r, int M, int N, int K, int bits, int words_per_row,
-             int lut_group_size, int lut_group_offset, int act_dtype, wlq_stream_t stream) {
+             int lut_group_size, int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream) {
     g_last_error[0] = '\0';
     LinearArgs a;
     int rc = build_args("wlq_gemm", X, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_H,
                         dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size, lut_group_offset,
-                        act_dtype, a);
+                        lut_format, act_dtype, a);
     if (rc) return rc;
     if (M == 0 || N == 0) return WLQ_OK;
     if ((rc = require_sm100())) return rc;
@@ -179,6 +183,52 @@ int wlq_dequant(const int32_t* q_packed, const void* lut_c, void* W_out, const i
                           has_outl ? chunk_cols : nullptr, has_outl ? chunk_vals : nullptr, N, K, bits, words_per_row,
                           lut_group_size, lut_group_offset, ngroups, chunk_m, (K + chunk_m - 1) / chunk_m,
                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wlq_prepack_lut(const void* lut_c, void* lut_out, int64_t n_codebooks, int act_dtype, wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    if (n_codebooks < 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_lut: negative count");
+    if (n_codebooks == 0) return WLQ_OK;
+    if (!lut_c || !lut_out) return fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_lut: null pointer");
+    if (act_dtype != WLQ_DTYPE_F16 && act_dtype != WLQ_DTYPE_BF16)
+        return fail(WLQ_ERR_UNSUPPORTED, "wlq_prepack_lut: act_dtype %d", act_dtype);
+    if (!aligned(lut_c, 16) || !aligned(lut_out, 16))
+        return fail(WLQ_ERR_ALIGNMENT, "wlq_prepack_lut: pointers must be 16-byte aligned");
+    const char* a = static_cast<const char*>(lut_c);
+    const char* b = static_cast<const char*>(lut_out);
+    if (a < b + n_codebooks * 32 && b < a + n_codebooks * 32)
+        return fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_lut: input and output overlap");
+    int rc = require_sm100();
+    if (rc) return rc;
+    return launch_prepack_lut(reinterpret_cast<const uint16_t*>(lut_c), reinterpret_cast<uint32_t*>(lut_out),
+                              n_codebooks, act_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wlq_prepack_outliers(const int32_t* q_packed, const void* lut_c, const int32_t* chunk_offsets,
+                         const uint16_t* chunk_cols, const uint8_t* chunk_vals, int64_t nnz, int N, int K, int bits,
+                         int words_per_row, int lut_group_size, int lut_group_offset, int act_dtype,
+                         uint16_t* cols_out, float* delta_out, wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    if (nnz < 0 || N < 0 || K < 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_outliers: negative size");
+    if (bits != 4) return fail(WLQ_ERR_UNSUPPORTED, "wlq_prepack_outliers: 4-bit indices only (bits=%d)", bits);
+    if (K > 65535) return fail(WLQ_ERR_UNSUPPORTED, "wlq_prepack_outliers: K=%d exceeds uint16 columns", K);
+    if (act_dtype != WLQ_DTYPE_F16 && act_dtype != WLQ_DTYPE_BF16)
+        return fail(WLQ_ERR_UNSUPPORTED, "wlq_prepack_outliers: act_dtype %d", act_dtype);
+    if (words_per_row != wlq::words_per_row(K, bits))
+        return fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_outliers: words_per_row does not match K");
+    if (lut_group_size < 0 || lut_group_offset < 0 || (lut_group_size > 0 && lut_group_offset >= lut_group_size))
+        return fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_outliers: bad codebook grouping");
+    if (nnz == 0 || N == 0) return WLQ_OK;
+    if (!q_packed || !lut_c || !chunk_offsets || !chunk_cols || !chunk_vals || !cols_out || !delta_out)
+        return fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_outliers: null pointer");
+    int rc = require_sm100();
+    if (rc) return rc;
+    const int chunk_m = chunk_m_for_bits(bits);
+    const int ngroups = lut_group_size > 0 ? (K + lut_group_offset + lut_group_size - 1) / lut_group_size : 1;
+    return launch_prepack_outliers(reinterpret_cast<const uint32_t*>(q_packed), reinterpret_cast<const uint16_t*>(lut_c),
+                                   chunk_offsets, chunk_cols, chunk_vals, N, K, words_per_row, lut_group_size,
+                                   lut_group_offset, ngroups, chunk_m, (K + chunk_m - 1) / chunk_m, act_dtype,
+                                   cols_out, delta_out, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device) {

@@ -303,3 +303,51 @@ int wlq_dequant_host(const int32_t* q_packed, const uint16_t* lut_c, uint16_t* W
 }
 
 }  // extern "C"
+
+namespace {
+// IEEE-754 binary16 -> binary32 (exact) and binary32 -> bfloat16 (round to
+// nearest even), from the formats' bit layouts.
+float f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t ex = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+    uint32_t bits;
+    if (ex == 0) {
+        float v = std::ldexp((float)man, -24);
+        std::memcpy(&bits, &v, 4);
+        bits |= sign;
+    } else if (ex == 31) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else {
+        bits = sign | ((ex + 112u) << 23) | (man << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+uint16_t f32_to_bf16(float f) {
+    uint32_t x;
+    std::memcpy(&x, &f, 4);
+    if ((x & 0x7F800000u) == 0x7F800000u && (x & 0x7FFFFFu)) return (uint16_t)((x >> 16) | 0x40u);
+    x += 0x7FFFu + ((x >> 16) & 1u);
+    return (uint16_t)(x >> 16);
+}
+}  // namespace
+
+extern "C" int wlq_prepack_lut_host(const uint16_t* lut_c, uint16_t* lut_out, int64_t n_codebooks, int act_dtype) {
+    if (n_codebooks < 0 || (n_codebooks > 0 && (!lut_c || !lut_out)) ||
+        (act_dtype != WLQ_DTYPE_F16 && act_dtype != WLQ_DTYPE_BF16))
+        return wlq::fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_lut_host: bad arguments");
+    for (int64_t i = 0; i < n_codebooks; ++i) {
+        uint16_t e[16];
+        for (int k = 0; k < 16; ++k) {
+            const uint16_t v = lut_c[i * 16 + k];
+            e[k] = act_dtype == WLQ_DTYPE_BF16 ? f32_to_bf16(f16_to_f32(v)) : v;
+        }
+        uint8_t* o = reinterpret_cast<uint8_t*>(lut_out + i * 16);
+        for (int k = 0; k < 16; ++k) {
+            o[k] = (uint8_t)(e[k] & 0xFFu);        // lo planes: entry k at byte k
+            o[16 + k] = (uint8_t)(e[k] >> 8);      // hi planes
+        }
+    }
+    return WLQ_OK;
+}

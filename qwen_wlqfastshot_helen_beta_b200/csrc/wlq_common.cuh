@@ -58,6 +58,14 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
     return r;
 }
 
+// Activations: re-read by every warp on the SM, keep them in L1.
+__device__ __forceinline__ uint4 ldg_keep_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::evict_last.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
 // Streaming load of weight index data: read once, do not keep in L1.
 __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
     uint4 r;

@@ -100,3 +100,101 @@ int launch_dequant(const uint32_t* q, const uint16_t* lut, uint16_t* W, const in
 }
 
 }  // namespace wlq
+
+// ---------------------------------------------------------------------------
+// Codebook prepacking (WLQ_LUT_PREPACKED): 16 fp16 entries -> entries in the
+// MMA type (fp16 unchanged, bf16 rounded to nearest even) split into byte
+// planes {lo[4], hi[4]}, the layout the GEMV/GEMM lookups permute from.
+// ---------------------------------------------------------------------------
+namespace wlq {
+
+template <typename T>
+__global__ void prepack_lut_kernel(const uint16_t* __restrict__ in, uint32_t* __restrict__ out, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint4 a = ldg_nc_v4(in + i * 16), b = ldg_nc_v4(in + i * 16 + 8);
+        uint32_t e[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        if (!ActTraits<T>::kIsF16) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&e[k]));
+                const __nv_bfloat162 v = __float22bfloat162_rn(f);
+                e[k] = *reinterpret_cast<const uint32_t*>(&v);
+            }
+        }
+        LutPlanes P;
+        make_planes(e, P);
+        uint4* dst = reinterpret_cast<uint4*>(out + i * 8);
+        dst[0] = make_uint4(P.lo[0], P.lo[1], P.lo[2], P.lo[3]);
+        dst[1] = make_uint4(P.hi[0], P.hi[1], P.hi[2], P.hi[3]);
+    }
+}
+
+int launch_prepack_lut(const uint16_t* in, uint32_t* out, int64_t n, int dtype, cudaStream_t stream) {
+    const int threads = 256;
+    int64_t blocks = (n + threads - 1) / threads;
+    const int64_t cap = (int64_t)device_sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    if (dtype == WLQ_DTYPE_BF16)
+        prepack_lut_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, stream>>>(in, out, n);
+    else
+        prepack_lut_kernel<__half><<<(unsigned)blocks, threads, 0, stream>>>(in, out, n);
+    return check_cuda(cudaGetLastError(), "prepack_lut_kernel launch");
+}
+
+}  // namespace wlq
+
+// ---------------------------------------------------------------------------
+// Outlier prepacking (WLQ_LUT_PREPACKED): chunk-CSR entries -> global column
+// (uint16) and the float32 correction w_outlier - codebook value as the MMA
+// sees it (codebook entry rounded to the MMA type), in the same order, so the
+// forward kernels add d * x without re-reading indices or codebooks.
+// ---------------------------------------------------------------------------
+namespace wlq {
+
+template <typename T>
+__global__ void prepack_outliers_kernel(const uint32_t* __restrict__ q, const uint16_t* __restrict__ lut,
+                                        const int32_t* __restrict__ off, const uint16_t* __restrict__ ccols,
+                                        const uint8_t* __restrict__ cvals, int N, int K, int wpr, int log2G,
+                                        bool grouped, int goff, int ngroups, int chunk_m, int ncsr,
+                                        uint16_t* __restrict__ gcols, float* __restrict__ delta) {
+    for (int row = blockIdx.x * blockDim.x + threadIdx.x; row < N; row += gridDim.x * blockDim.x) {
+        const int32_t* ro = off + (int64_t)row * (ncsr + 1);
+        for (int cc = 0; cc < ncsr; ++cc) {
+            for (int i = ro[cc]; i < ro[cc + 1]; ++i) {
+                const int col = cc * chunk_m + ccols[i];
+                float d = 0.f;
+                if (col < K) {
+                    const uint32_t sym = (q[(int64_t)row * wpr + (col >> 3)] >> (4 * (col & 7))) & 15u;
+                    const int grp = grouped ? (col + goff) >> log2G : 0;
+                    const uint16_t lb = lut[((int64_t)row * ngroups + grp) * 16 + sym];
+                    const float wl = ActTraits<T>::bits_to_f32(ActTraits<T>::from_f16_bits(lb));
+                    d = f16_bits_to_f32(fp8_byte_to_f16_bits(cvals[i])) - wl;
+                }
+                gcols[i] = (uint16_t)(col < K ? col : 0xFFFF);  // 0xFFFF: dropped (past K)
+                delta[i] = d;
+            }
+        }
+    }
+}
+
+int launch_prepack_outliers(const uint32_t* q, const uint16_t* lut, const int32_t* off, const uint16_t* ccols,
+                            const uint8_t* cvals, int N, int K, int wpr, int group_size, int goff, int ngroups,
+                            int chunk_m, int ncsr, int dtype, uint16_t* gcols, float* delta, cudaStream_t stream) {
+    int log2G = 0;
+    if (group_size > 0) {
+        while ((1 << log2G) < group_size) ++log2G;
+        if ((1 << log2G) != group_size)
+            return fail(WLQ_ERR_UNSUPPORTED, "wlq_prepack_outliers: group_size must be a power of two");
+    }
+    const int threads = 128;
+    const int blocks = (N + threads - 1) / threads;
+    if (dtype == WLQ_DTYPE_BF16)
+        prepack_outliers_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(
+            q, lut, off, ccols, cvals, N, K, wpr, log2G, group_size > 0, goff, ngroups, chunk_m, ncsr, gcols, delta);
+    else
+        prepack_outliers_kernel<__half><<<blocks, threads, 0, stream>>>(
+            q, lut, off, ccols, cvals, N, K, wpr, log2G, group_size > 0, goff, ngroups, chunk_m, ncsr, gcols, delta);
+    return check_cuda(cudaGetLastError(), "prepack_outliers_kernel launch");
+}
+
+}  // namespace wlq

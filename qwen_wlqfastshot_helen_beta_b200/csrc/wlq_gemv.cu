@@ -4,24 +4,32 @@
 // (csrc/gemv_kernel.cu:86-353) and, for 2 <= M <= 16, the wmma kernel
 // (csrc/gemm_kernel.cu:32-294).
 //
-// The kernel is HBM-bound (0.5 B of indices per weight, +0.25 B with 128-wide
-// per-group codebooks), so the design goal is the fewest instructions per
-// weight:
+// HBM-bound: 0.5 B of indices per weight (+0.25 B with 128-wide per-group
+// codebooks).  On B200 the integer/logic pipe retires 64 lanes per clock per
+// SM, so the lookup must stay near 2 such instructions per weight:
 //  * the tensor core does the multiply-accumulate: weights are the A operand
 //    of mma.m16n8k16 (16 output rows x 16 k), tokens the 8-wide B operand;
-//    one MMA retires 256 weights for up to 8 tokens;
-//  * the codebook lookup runs in registers through byte permutes (LutPlanes),
-//    no shared memory traffic per weight;
+//  * the codebook lookup runs in registers through byte permutes (LutPlanes):
+//    8 permutes per 4 weights plus 2 logic ops per 8; the shifts that feed
+//    the upper index halves run as mul.hi on the FMA pipe;
+//  * codebooks arrive as byte planes already in the MMA type ("prepacked",
+//    wlq_prepack_lut) so the hot loop never converts or rebuilds them; the
+//    reference fp16 layout is accepted too and rebuilt per lane;
 //  * the A fragment's k order is free (the same permutation is applied to x):
 //    lane (g, t) owns rows g and g+8 and the 32 consecutive columns
 //    [32t, 32t+32) of every 128-wide chunk, so it reads 16 contiguous bytes of
-//    each of its rows per chunk with one 128-bit load;
-//  * K is split over the 4 warps of a CTA and over the CTAs of a thread-block
-//    cluster; partial sums meet in shared memory and, across the cluster, in
-//    distributed shared memory, so no global workspace and no second launch.
-// Outliers REPLACE the codebook weight (csrc/gemm_kernel.cu:204-228); here the
-// replacement is applied as (w_outlier - w_codebook) * x after the MMA loop,
-// the same arithmetic as csrc/gemv_kernel.cu:262-288.
+//    each of its rows per chunk with one 128-bit load; DEPTH chunks of index
+//    words and the next chunk's codebooks are in flight per lane;
+//  * the CTA stages its K range of the activations in shared memory once
+//    (cp.async), so the B fragments are short-latency shared loads;
+//  * each warp owns a 16-row tile; K is split only across the CTAs of a
+//    thread-block cluster, whose partial tiles meet in distributed shared
+//    memory: no global workspace, no second launch.
+// Outliers REPLACE the codebook weight (csrc/gemm_kernel.cu:204-228).  After
+// the MMA loop each warp adds (w_outlier - w_codebook) * x for the outliers of
+// its tile (the arithmetic of csrc/gemv_kernel.cu:262-288): two lanes per row
+// walk the row's chunk-CSR entries, accumulate in registers and combine with
+// one shuffle.
 #include "wlq_common.cuh"
 #include "wlq_internal.h"
 
@@ -46,86 +54,139 @@ struct GemvParams {
     const uint16_t* gamma;
     float scale;
     int r, M, N, K, wpr, G, goff, ngroups, chunk_m, ncsr;
-    int kchunks;          // ceil(K / 128)
-    int chunks_per_warp;  // K split granularity
-    int xvec;             // rows of x are 16-byte aligned (K % 8 == 0)
+    int log2G;             // group_size = 1 << log2G when grouped
+    int kchunks;           // ceil(K / 128)
+    int chunks_per_rank;   // K split across the cluster
+    int x_stride;          // shared-memory row stride of staged activations (elements)
+    uint32_t mul16, mul31; // 1<<16 and 1<<31, runtime values so mul.hi stays a multiply
 };
 
-template <typename T>
+// x >> 16 and x >> 1 on the FMA pipe (mul.hi by a runtime power of two).
+__device__ __forceinline__ uint32_t mulhi(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+    return d;
+}
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(m), "r"(o));  // (a & m) | o
+    return d;
+}
+
+// (T[q0],T[q1]) and (T[q2],T[q3]) for the four indices in the low 16 bits.
+__device__ __forceinline__ void lookup4(const LutPlanes& p, uint32_t sel, uint32_t csel, uint32_t& o01,
+                                        uint32_t& o23) {
+    const uint32_t la = prmt(p.lo[0], p.lo[1], sel);
+    const uint32_t lb = prmt(p.lo[2], p.lo[3], sel);
+    const uint32_t ha = prmt(p.hi[0], p.hi[1], sel);
+    const uint32_t hb = prmt(p.hi[2], p.hi[3], sel);
+    const uint32_t lo = prmt(la, lb, csel);
+    const uint32_t hi = prmt(ha, hb, csel);
+    o01 = prmt(lo, hi, 0x5140u);
+    o23 = prmt(lo, hi, 0x7362u);
+}
+
+// Codebook planes of one (row, group): prepacked (8 words: lo[4], hi[4]) or
+// the reference's 16 fp16 entries, converted and permuted here.
+template <typename T, bool PREPACKED>
 __device__ __forceinline__ void load_planes(const uint16_t* __restrict__ lut, int64_t entry, bool valid,
                                             LutPlanes& P) {
-    uint32_t e[8];
-    if (valid) {
-        const uint4 a = ldg_nc_v4(lut + entry * 16);
-        const uint4 b = ldg_nc_v4(lut + entry * 16 + 8);
-        e[0] = a.x; e[1] = a.y; e[2] = a.z; e[3] = a.w;
-        e[4] = b.x; e[5] = b.y; e[6] = b.z; e[7] = b.w;
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) e[i] = 0u;
+    uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
+    if (valid) {  // streamed: the 4 lanes sharing a codebook read it in one request
+        a = ldg_stream_v4(lut + entry * 16);
+        b = ldg_stream_v4(lut + entry * 16 + 8);
     }
+    if (PREPACKED) {
+        P.lo[0] = a.x; P.lo[1] = a.y; P.lo[2] = a.z; P.lo[3] = a.w;
+        P.hi[0] = b.x; P.hi[1] = b.y; P.hi[2] = b.z; P.hi[3] = b.w;
+        return;
+    }
+    uint32_t e[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     if (!ActTraits<T>::kIsF16) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint32_t lo = ActTraits<T>::from_f16_bits((uint16_t)(e[i] & 0xFFFFu));
-            const uint32_t hi = ActTraits<T>::from_f16_bits((uint16_t)(e[i] >> 16));
-            e[i] = lo | (hi << 16);
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&e[i]));
+            const __nv_bfloat162 v = __float22bfloat162_rn(f);
+            e[i] = *reinterpret_cast<const uint32_t*>(&v);
         }
     }
     make_planes(e, P);
 }
 
-// 32 consecutive activations of one token starting at column k (zero beyond
-// K or for an absent token).
-template <typename T>
-__device__ __forceinline__ void load_x32(const T* __restrict__ x, int tok, int M, int K, int k, int xvec,
-                                         uint4 xv[4]) {
-#pragma unroll
-    for (int v = 0; v < 4; ++v) xv[v] = make_uint4(0u, 0u, 0u, 0u);
-    if (tok >= M) return;
-    const T* xr = x + (int64_t)tok * K;
-    if (xvec) {  // K % 8 == 0: each 8-wide group is wholly inside or outside K
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-            if (k + 8 * v + 8 <= K) xv[v] = ldg_nc_v4(xr + k + 8 * v);
-        return;
+// Codebook value of symbol q of one (row, group) as the MMA saw it.
+template <typename T, bool PREPACKED>
+__device__ __forceinline__ float codebook_value(const uint16_t* __restrict__ lut, int64_t entry, uint32_t q) {
+    if (PREPACKED) {
+        const uint8_t* rec = reinterpret_cast<const uint8_t*>(lut + entry * 16);
+        const uint16_t bits = (uint16_t)(__ldg(rec + q) | ((uint16_t)__ldg(rec + 16 + q) << 8));
+        return ActTraits<T>::bits_to_f32(bits);
     }
-    const uint16_t* xs = reinterpret_cast<const uint16_t*>(xr);
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-        uint32_t w[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int k0 = k + 8 * v + 2 * j;
-            const uint32_t lo = k0 < K ? (uint32_t)__ldg(xs + k0) : 0u;
-            const uint32_t hi = k0 + 1 < K ? (uint32_t)__ldg(xs + k0 + 1) : 0u;
-            w[j] = lo | (hi << 16);
-        }
-        xv[v] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
+    return ActTraits<T>::bits_to_f32(ActTraits<T>::from_f16_bits(__ldg(lut + entry * 16 + q)));
 }
 
-template <typename T, int MT, bool GROUPED>
-__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvParams p) {
-    constexpr int NT = MT / 8;  // n8 tiles of tokens
-    __shared__ float red[kWarps][kRowsPerTile][MT];
-    __shared__ float part[kRowsPerTile * MT];
+// Stages x[0:M, kb:kb+cols) into shared memory, rows padded by 8 elements
+// (16 bytes) so the per-token rows fall in different banks; columns past K
+// read as zero.  16-byte cp.async when rows of x are 16-byte aligned.
+template <typename T, bool XVEC>
+__device__ __forceinline__ void stage_x(uint16_t* xs, const T* __restrict__ x, int M, int K, int kb, int cols,
+                                        int stride) {
+    const uint16_t* xg = reinterpret_cast<const uint16_t*>(x);
+    const int pieces = cols / 8;
+    for (int e = threadIdx.x; e < M * pieces; e += blockDim.x) {
+        const int m = e / pieces, pc = e - m * pieces;
+        const int k = kb + 8 * pc;
+        uint16_t* dst = xs + m * stride + 8 * pc;
+        if (XVEC && k + 8 <= K) {
+            const uint32_t sa = smem_u32(dst);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(xg + (int64_t)m * K + k) : "memory");
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[j] = k + j < K ? xg[(int64_t)m * K + k + j] : (uint16_t)0;
+        }
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+template <typename T, int NT, bool GROUPED, bool PREPACKED, bool XVEC, bool XSMEM, int DEPTH>
+__global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p) {
+    constexpr int MT = 8 * NT;
+    extern __shared__ __align__(16) uint16_t xs[];  // [M][x_stride] activations of this rank's K range
+    static_assert(DEPTH % 2 == 0, "the codebook ring alternates slots with chunk parity");
+    __shared__ float part[kWarps][kRowsPerTile][MT];  // per-warp partial tile
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2;
     const int t = lane & 3;
-    const int row0 = blockIdx.x * kRowsPerTile + g;
+    const int tile_row0 = (blockIdx.x * kWarps + warp) * kRowsPerTile;
+    const int row0 = tile_row0 + g;
     const int row1 = row0 + 8;
     const bool v0 = row0 < p.N;
     const bool v1 = row1 < p.N;
     const uint32_t* q0 = p.q + (int64_t)(v0 ? row0 : 0) * p.wpr;
     const uint32_t* q1 = p.q + (int64_t)(v1 ? row1 : 0) * p.wpr;
     const T* x = reinterpret_cast<const T*>(p.x);
+    const uint32_t m16 = p.mul16, m31 = p.mul31;
+    const int64_t cb0 = (int64_t)(v0 ? row0 : 0) * p.ngroups;  // codebook entry base of each row
+    const int64_t cb1 = (int64_t)(v1 ? row1 : 0) * p.ngroups;
 
-    const int slice = blockIdx.y * kWarps + warp;
-    const int c_begin = slice * p.chunks_per_warp;
-    const int c_end = min(p.kchunks, c_begin + p.chunks_per_warp);
+    const int c_begin = blockIdx.y * p.chunks_per_rank;
+    const int c_end = min(p.kchunks, c_begin + p.chunks_per_rank);
+
+    uint4 wa[DEPTH], wb[DEPTH];
+#pragma unroll
+    for (int j = 0; j < DEPTH; ++j) {
+        const int c = c_begin + j;
+        const int wi = c * (kChunk / 8) + 4 * t;
+        const bool in = c < c_end && wi < p.wpr;
+        wa[j] = (v0 && in) ? ldg_stream_v4(q0 + wi) : make_uint4(0u, 0u, 0u, 0u);
+        wb[j] = (v1 && in) ? ldg_stream_v4(q1 + wi) : make_uint4(0u, 0u, 0u, 0u);
+    }
 
     float acc[NT][4];
 #pragma unroll
@@ -133,138 +194,200 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvParams p) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
 
-    LutPlanes P0, P1;
-    int cur_grp = -1;
-    if (!GROUPED) {
-        load_planes<T>(p.lut, v0 ? row0 : 0, v0, P0);
-        load_planes<T>(p.lut, v1 ? row1 : 0, v1, P1);
+    // this rank's activations into shared memory (index words already in flight)
+    // (XSMEM) or read them from L1 when the slice is too large to stage
+    const int kb0 = c_begin * kChunk;
+    if (XSMEM) {
+        stage_x<T, XVEC>(xs, x, p.M, p.K, kb0, p.chunks_per_rank * kChunk, p.x_stride);
+        __syncthreads();
+    }
+    bool tok_ok[NT];
+    const uint16_t* xrow[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        tok_ok[j] = 8 * j + g < p.M;
+        const int tok = tok_ok[j] ? 8 * j + g : 0;
+        xrow[j] = XSMEM ? xs + tok * p.x_stride + 32 * t  // this lane's 32 columns of chunk c_begin
+                        : reinterpret_cast<const uint16_t*>(x) + (int64_t)tok * p.K + kb0 + 32 * t;
     }
 
-    // software pipeline: the next chunk's index words are in flight while
-    // the current chunk is dequantised and multiplied
-    uint4 w0n = make_uint4(0u, 0u, 0u, 0u), w1n = w0n;
-    auto load_words = [&](int c, uint4& a, uint4& b) {
-        const int wi = c * (kChunk / 8) + 4 * t;
-        const bool in = wi < p.wpr;
-        a = (v0 && in) ? ldg_stream_v4(q0 + wi) : make_uint4(0u, 0u, 0u, 0u);
-        b = (v1 && in) ? ldg_stream_v4(q1 + wi) : make_uint4(0u, 0u, 0u, 0u);
-    };
-    if (c_begin < c_end) load_words(c_begin, w0n, w1n);
+    // codebook of this lane's 32 columns of chunk c (lanes past K are clamped:
+    // they multiply zero activations)
+    auto group_of = [&](int c) { return min((c * kChunk + 32 * t + p.goff) >> p.log2G, p.ngroups - 1); };
+    LutPlanes PL[2][2];  // [slot][row0/row1]
+    if (!GROUPED) {
+        load_planes<T, PREPACKED>(p.lut, cb0, v0, PL[0][0]);
+        load_planes<T, PREPACKED>(p.lut, cb1, v1, PL[0][1]);
+    } else if (c_begin < c_end) {
+        const int gg = group_of(c_begin);
+        load_planes<T, PREPACKED>(p.lut, cb0 + gg, v0, PL[0][0]);
+        load_planes<T, PREPACKED>(p.lut, cb1 + gg, v1, PL[0][1]);
+    }
 
-    for (int c = c_begin; c < c_end; ++c) {
-        const uint4 w0 = w0n, w1 = w1n;
-        if (c + 1 < c_end) load_words(c + 1, w0n, w1n);
-        const int kl = c * kChunk + 32 * t;  // first column of this lane
-        uint4 xa[NT][4];
+    // activations (shared memory) run one k-step pair ahead of their use
+    auto lds_x8 = [&](int tt, int off) -> uint4 {
+        if (!tok_ok[tt]) return make_uint4(0u, 0u, 0u, 0u);
+        if (XSMEM) return *reinterpret_cast<const uint4*>(xrow[tt] + off);
+        const int k = kb0 + 32 * t + off;  // global column of this 8-wide piece
+        if (XVEC) return k + 8 <= p.K ? ldg_keep_v4(xrow[tt] + off) : make_uint4(0u, 0u, 0u, 0u);
+        uint32_t w[4];
 #pragma unroll
-        for (int j = 0; j < NT; ++j) load_x32<T>(x, 8 * j + g, p.M, p.K, kl, p.xvec, xa[j]);
-        if (GROUPED) {
-            // lanes past K multiply zero activations; clamp their group so the
-            // codebook read stays inside the row
-            const int grp = min((kl + p.goff) / p.G, p.ngroups - 1);
-            if (grp != cur_grp) {
-                cur_grp = grp;
-                load_planes<T>(p.lut, (int64_t)(v0 ? row0 : 0) * p.ngroups + grp, v0, P0);
-                load_planes<T>(p.lut, (int64_t)(v1 ? row1 : 0) * p.ngroups + grp, v1, P1);
-            }
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = k + 2 * j < p.K ? (uint32_t)__ldg(xrow[tt] + off + 2 * j) : 0u;
+            const uint32_t hi = k + 2 * j + 1 < p.K ? (uint32_t)__ldg(xrow[tt] + off + 2 * j + 1) : 0u;
+            w[j] = lo | (hi << 16);
         }
-        const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
-        const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    };
+    auto x_at = [&](int m, int col) -> float {  // activation of token m at global column col
+        return XSMEM ? ActTraits<T>::bits_to_f32(xs[m * p.x_stride + col - kb0])
+                     : ActTraits<T>::to_f32(x[(int64_t)m * p.K + col]);
+    };
+    uint4 xnext[NT];
 #pragma unroll
-        for (int ws = 0; ws < 4; ++ws) {
-            uint32_t sa, ca, sb, cb;
-            lut_selectors(wa[ws], sa, ca);
-            lut_selectors(wb[ws], sb, cb);
+    for (int tt = 0; tt < NT; ++tt) xnext[tt] = c_begin < c_end ? lds_x8(tt, 0) : make_uint4(0u, 0u, 0u, 0u);
+
+    for (int cb = c_begin; cb < c_end; cb += DEPTH) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t a[4];
-                lut4(P0, sa, ca, a[0], a[2]);
-                lut4(P1, sb, cb, a[1], a[3]);
-                sa >>= 16; ca >>= 16; sb >>= 16; cb >>= 16;
+        for (int j = 0; j < DEPTH; ++j) {
+            const int c = cb + j;
+            if (c >= c_end) break;
+            const int slot = GROUPED ? (j & 1) : 0;
+            const uint4 w0 = wa[j], w1 = wb[j];
+            {  // refill this slot with chunk c + DEPTH
+                const int cn = c + DEPTH;
+                const int wi = cn * (kChunk / 8) + 4 * t;
+                const bool in = cn < c_end && wi < p.wpr;
+                wa[j] = (v0 && in) ? ldg_stream_v4(q0 + wi) : make_uint4(0u, 0u, 0u, 0u);
+                wb[j] = (v1 && in) ? ldg_stream_v4(q1 + wi) : make_uint4(0u, 0u, 0u, 0u);
+            }
+            if (GROUPED && c + 1 < c_end) {  // next chunk's codebooks into the other slot
+                const int gg = group_of(c + 1);
+                load_planes<T, PREPACKED>(p.lut, cb0 + gg, v0, PL[slot ^ 1][0]);
+                load_planes<T, PREPACKED>(p.lut, cb1 + gg, v1, PL[slot ^ 1][1]);
+            }
+            const uint32_t ra[4] = {w0.x, w0.y, w0.z, w0.w};
+            const uint32_t rb[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-                for (int j = 0; j < NT; ++j) {
-                    const uint32_t b0 = h ? xa[j][ws].z : xa[j][ws].x;
-                    const uint32_t b1 = h ? xa[j][ws].w : xa[j][ws].y;
-                    Mma16816<T>::run(acc[j], a, b0, b1);
+            for (int ws = 0; ws < 4; ++ws) {
+                uint4 xv[NT];
+#pragma unroll
+                for (int tt = 0; tt < NT; ++tt) {
+                    xv[tt] = xnext[tt];
+                    // next pair: this chunk's ws+1, or the next chunk's first
+                    const int kn = (c - c_begin) * kChunk + (ws < 3 ? 8 * (ws + 1) : kChunk);
+                    if (ws < 3 || c + 1 < c_end) xnext[tt] = lds_x8(tt, kn);
+                }
+                const uint32_t sa = ra[ws] & 0x77777777u;
+                const uint32_t ca = lop_and_or(mulhi(ra[ws], m31), 0x44444444u, 0x32103210u);
+                const uint32_t sb = rb[ws] & 0x77777777u;
+                const uint32_t cb2 = lop_and_or(mulhi(rb[ws], m31), 0x44444444u, 0x32103210u);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t a[4];
+                    if (h == 0) {
+                        lookup4(PL[slot][0], sa, ca, a[0], a[2]);
+                        lookup4(PL[slot][1], sb, cb2, a[1], a[3]);
+                    } else {
+                        lookup4(PL[slot][0], mulhi(sa, m16), mulhi(ca, m16), a[0], a[2]);
+                        lookup4(PL[slot][1], mulhi(sb, m16), mulhi(cb2, m16), a[1], a[3]);
+                    }
+#pragma unroll
+                    for (int tt = 0; tt < NT; ++tt) {
+                        const uint32_t b0 = h ? xv[tt].z : xv[tt].x;
+                        const uint32_t b1 = h ? xv[tt].w : xv[tt].y;
+                        Mma16816<T>::run(acc[tt], a, b0, b1);
+                    }
                 }
             }
         }
     }
 
-    // outlier replacement for this warp's K range: (w_outlier - w_codebook) * x
+    // publish this warp's partial tile
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            part[warp][g][8 * tt + 2 * t + e] = acc[tt][e];
+            part[warp][g + 8][8 * tt + 2 * t + e] = acc[tt][2 + e];
+        }
+    __syncwarp();
+
+    // outlier replacement over this rank's K range: lanes l and l+16 share
+    // tile row l % 16 and take alternate entries of its chunk-CSR range
     if (p.off != nullptr && c_begin < c_end) {
         const int kb = c_begin * kChunk;
         const int ke = min(p.K, c_end * kChunk);
+        const int rl = lane & 15;
+        const int row = tile_row0 + rl;
+        float os[MT];
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-            const int row = rr ? row1 : row0;
-            if (!(rr ? v1 : v0)) continue;
-            const uint32_t* qr = rr ? q1 : q0;
-            const int cc_lo = kb / p.chunk_m;
-            const int cc_hi = (ke - 1) / p.chunk_m;
-            for (int cc = cc_lo; cc <= cc_hi; ++cc) {
-                const int64_t ob = (int64_t)row * (p.ncsr + 1) + cc;
-                const int ia = __ldg(p.off + ob), ib = __ldg(p.off + ob + 1);
-                for (int i = ia; i < ib; ++i) {
-                    const int col = cc * p.chunk_m + (int)__ldg(p.ccols + i);
-                    if (col < kb || col >= ke) continue;
-                    const uint32_t sym = (__ldg(qr + (col >> 3)) >> (4 * (col & 7))) & 15u;
-                    const int grp = GROUPED ? (col + p.goff) / p.G : 0;
-                    const uint16_t lb = __ldg(p.lut + ((int64_t)row * p.ngroups + grp) * 16 + sym);
-                    // the codebook value the MMA used (rounded to bf16 on the bf16 path)
-                    const float wl = ActTraits<T>::bits_to_f32(ActTraits<T>::from_f16_bits(lb));
-                    const float wo = f16_bits_to_f32(fp8_byte_to_f16_bits(__ldg(p.cvals + i)));
-                    const float d = wo - wl;
+        for (int m = 0; m < MT; ++m) os[m] = 0.f;
+        if (PREPACKED && row < p.N) {
+            // global columns and ready corrections: two independent loads per
+            // entry, then the activations; four entries in flight per lane
+            const int32_t* ro = p.off + (int64_t)row * (p.ncsr + 1);
+            const int ia = __ldg(ro + kb / p.chunk_m), ib = __ldg(ro + (ke - 1) / p.chunk_m + 1);
+            const float* dl = reinterpret_cast<const float*>(p.cvals);
+            for (int i0 = ia + (lane >> 4); i0 < ib; i0 += 8) {
+                int col[4];
+                float d[4];
 #pragma unroll
-                    for (int j = 0; j < NT; ++j)
+                for (int u = 0; u < 4; ++u) {
+                    const int i = i0 + 2 * u;
+                    col[u] = i < ib ? (int)__ldg(p.ccols + i) : -1;
+                    d[u] = i < ib ? __ldg(dl + i) : 0.f;
+                }
 #pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const int m = 8 * j + 2 * t + e;
-                            if (m < p.M) acc[j][2 * rr + e] += d * ActTraits<T>::to_f32(x[(int64_t)m * p.K + col]);
-                        }
+                for (int u = 0; u < 4; ++u) {
+                    if (col[u] < kb || col[u] >= ke) continue;
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                        if (m < p.M) os[m] += d[u] * x_at(m, col[u]);
                 }
             }
+        } else if (row < p.N) {
+            const int32_t* ro = p.off + (int64_t)row * (p.ncsr + 1);
+            int cc = kb / p.chunk_m;
+            const int cc_hi = (ke - 1) / p.chunk_m;
+            int bound = __ldg(ro + cc + 1);  // end of chunk cc
+            const int ib = __ldg(ro + cc_hi + 1);
+            for (int i = __ldg(ro + cc) + (lane >> 4); i < ib; i += 2) {
+                while (i >= bound) bound = __ldg(ro + (++cc) + 1);  // entries are chunk-ordered
+                const int col = cc * p.chunk_m + (int)__ldg(p.ccols + i);
+                if (col < kb || col >= ke) continue;
+                const uint32_t sym = (__ldg(p.q + (int64_t)row * p.wpr + (col >> 3)) >> (4 * (col & 7))) & 15u;
+                const int grp = GROUPED ? ((col + p.goff) >> p.log2G) : 0;
+                const float wl = codebook_value<T, PREPACKED>(p.lut, (int64_t)row * p.ngroups + grp, sym);
+                const float d = f16_bits_to_f32(fp8_byte_to_f16_bits(__ldg(p.cvals + i))) - wl;
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                    if (m < p.M) os[m] += d * x_at(m, col);
+            }
         }
-    }
-
-    // reduce the 4 warps' partial tiles
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-        red[warp][g][8 * j + 2 * t] = acc[j][0];
-        red[warp][g][8 * j + 2 * t + 1] = acc[j][1];
-        red[warp][g + 8][8 * j + 2 * t] = acc[j][2];
-        red[warp][g + 8][8 * j + 2 * t + 1] = acc[j][3];
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < kRowsPerTile * MT; e += blockDim.x) {
-        const int rl = e / MT, tk = e % MT;
-        float s = 0.f;
+        for (int m = 0; m < MT; ++m) os[m] += __shfl_down_sync(0xFFFFFFFFu, os[m], 16);
+        if (lane < 16) {
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) s += red[w][rl][tk];
-        part[e] = s;
+            for (int m = 0; m < MT; ++m) part[warp][rl][m] += os[m];
+        }
+        __syncwarp();
     }
 
     const bool clustered = gridDim.y > 1;
-    if (clustered) {
-        // all CTAs of the cluster publish `part`; rank 0 sums them through
-        // distributed shared memory and writes the output
-        cluster_sync_all();
-    } else {
-        __syncthreads();
-    }
+    if (clustered) cluster_sync_all();  // every rank's partial tiles are visible cluster-wide
     const uint32_t rank = clustered ? cluster_ctarank() : 0u;
     if (rank == 0) {
         const uint32_t nranks = clustered ? cluster_nctarank() : 1u;
         const bool dora = p.r > 0;
-        for (int e = threadIdx.x; e < kRowsPerTile * MT; e += blockDim.x) {
+        for (int e = lane; e < kRowsPerTile * MT; e += 32) {
             const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;  // rows fastest: coalesced stores
-            const int n = blockIdx.x * kRowsPerTile + rl;
+            const int n = tile_row0 + rl;
             if (n >= p.N || tk >= p.M) continue;
-            const int pe = rl * MT + tk;
-            float s = part[pe];
+            float s = part[warp][rl][tk];
             if (clustered) {
-                const uint32_t a = smem_u32(&part[pe]);
-                for (uint32_t q = 1; q < nranks; ++q) s += ld_shared_cluster_f32(mapa_shared(a, q));
+                const uint32_t a = smem_u32(&part[warp][rl][tk]);
+                for (uint32_t qq = 1; qq < nranks; ++qq) s += ld_shared_cluster_f32(mapa_shared(a, qq));
             }
             if (dora) {
                 float l = 0.f;
@@ -276,15 +399,22 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvParams p) {
             reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s);
         }
     }
-    if (clustered) cluster_sync_all();  // keep every CTA's `part` alive until rank 0 is done
+    if (clustered) cluster_sync_all();  // keep every rank's tiles alive until rank 0 is done
 }
 
-template <typename T, int MT, bool GROUPED>
-int launch_variant(const GemvParams& p, int row_tiles, int cs, cudaStream_t stream) {
+template <typename T, int NT, bool GROUPED, bool PREPACKED, bool XVEC, bool XSMEM>
+int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream) {
+    constexpr int DEPTH = NT == 1 ? 4 : 2;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)row_tiles, (unsigned)cs, 1);
+    cfg.gridDim = dim3((unsigned)ctas, (unsigned)cs, 1);
     cfg.blockDim = dim3(kWarps * 32, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    const size_t smem = XSMEM ? (size_t)p.M * p.x_stride * 2 : 0;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(gemv_kernel<T, NT, GROUPED, PREPACKED, XVEC, XSMEM, DEPTH>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return check_cuda(e, "gemv_kernel smem attribute");
+    }
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -293,18 +423,33 @@ int launch_variant(const GemvParams& p, int row_tiles, int cs, cudaStream_t stre
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = cs > 1 ? 1 : 0;
-    return check_cuda(cudaLaunchKernelEx(&cfg, gemv_kernel<T, MT, GROUPED>, p), "gemv_kernel launch");
+    return check_cuda(cudaLaunchKernelEx(&cfg, gemv_kernel<T, NT, GROUPED, PREPACKED, XVEC, XSMEM, DEPTH>, p),
+                      "gemv_kernel launch");
+}
+
+template <typename T, int NT, bool GROUPED, bool PREPACKED>
+int dispatch_x(const GemvParams& p, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+    if (xsmem)
+        return xvec ? launch_variant<T, NT, GROUPED, PREPACKED, true, true>(p, ctas, cs, stream)
+                    : launch_variant<T, NT, GROUPED, PREPACKED, false, true>(p, ctas, cs, stream);
+    return xvec ? launch_variant<T, NT, GROUPED, PREPACKED, true, false>(p, ctas, cs, stream)
+                : launch_variant<T, NT, GROUPED, PREPACKED, false, false>(p, ctas, cs, stream);
+}
+
+template <typename T, int NT, bool GROUPED>
+int dispatch_fmt(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+    return prepacked ? dispatch_x<T, NT, GROUPED, true>(p, xvec, xsmem, ctas, cs, stream)
+                     : dispatch_x<T, NT, GROUPED, false>(p, xvec, xsmem, ctas, cs, stream);
 }
 
 template <typename T>
-int dispatch(const GemvParams& p, int row_tiles, int cs, cudaStream_t stream) {
+int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
     const bool grouped = p.G > 0;
-    if (p.M <= 8) {
-        return grouped ? launch_variant<T, 8, true>(p, row_tiles, cs, stream)
-                       : launch_variant<T, 8, false>(p, row_tiles, cs, stream);
-    }
-    return grouped ? launch_variant<T, 16, true>(p, row_tiles, cs, stream)
-                   : launch_variant<T, 16, false>(p, row_tiles, cs, stream);
+    if (p.M <= 8)
+        return grouped ? dispatch_fmt<T, 1, true>(p, prepacked, xvec, xsmem, ctas, cs, stream)
+                       : dispatch_fmt<T, 1, false>(p, prepacked, xvec, xsmem, ctas, cs, stream);
+    return grouped ? dispatch_fmt<T, 2, true>(p, prepacked, xvec, xsmem, ctas, cs, stream)
+                   : dispatch_fmt<T, 2, false>(p, prepacked, xvec, xsmem, ctas, cs, stream);
 }
 
 }  // namespace
@@ -312,28 +457,40 @@ int dispatch(const GemvParams& p, int row_tiles, int cs, cudaStream_t stream) {
 int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     if (a.M == 0 || a.N == 0) return WLQ_OK;
     if (a.M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: M must be <= 16, got %d", a.M);
-    if (a.group_size > 0 && (a.group_size % 32 != 0 || a.group_offset % 32 != 0))
-        return fail(WLQ_ERR_UNSUPPORTED,
-                    "wlq_gemv: per-group codebooks need group_size and group_offset multiples of 32 "
-                    "(got %d, %d)", a.group_size, a.group_offset);
+    int log2G = 0;
+    if (a.group_size > 0) {
+        while ((1 << log2G) < a.group_size) ++log2G;
+        if ((1 << log2G) != a.group_size || a.group_size < 32 || a.group_offset % 32 != 0)
+            return fail(WLQ_ERR_UNSUPPORTED,
+                        "wlq_gemv: per-group codebooks need a power-of-two group_size >= 32 and a group_offset "
+                        "multiple of 32 (got %d, %d)", a.group_size, a.group_offset);
+    }
     GemvParams p;
     p.q = a.q; p.lut = a.lut; p.x = a.x; p.out = a.out;
     p.off = a.off; p.ccols = a.ccols; p.cvals = a.cvals;
     p.loraB = a.loraB; p.lorah = a.lorah; p.gamma = a.gamma; p.scale = a.scale; p.r = a.r;
     p.M = a.M; p.N = a.N; p.K = a.K; p.wpr = a.wpr; p.G = a.group_size; p.goff = a.group_offset;
     p.ngroups = a.ngroups; p.chunk_m = a.chunk_m; p.ncsr = a.ncsr;
+    p.log2G = log2G;
     p.kchunks = (a.K + kChunk - 1) / kChunk;
-    p.xvec = (a.K % 8 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
+    p.mul16 = 1u << 16;
+    p.mul31 = 1u << 31;
+    const bool xvec = (a.K % 8 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
 
-    const int row_tiles = (a.N + kRowsPerTile - 1) / kRowsPerTile;
-    // Split K over a cluster until about 4 CTAs per SM are in flight, keeping
-    // at least 2 chunks per warp.
+    const int tiles = (a.N + kRowsPerTile - 1) / kRowsPerTile;
+    const int ctas = (tiles + kWarps - 1) / kWarps;
+    // Split K over a cluster until about 4 CTAs (16 warps) per SM are in
+    // flight, keeping at least 2 chunks per rank.
     const int sms = device_sm_count();
     int cs = 1;
-    while (cs < 8 && (int64_t)row_tiles * cs < 4LL * sms && p.kchunks >= 2 * kWarps * (cs + 1)) ++cs;
-    p.chunks_per_warp = (p.kchunks + kWarps * cs - 1) / (kWarps * cs);
-    if (a.dtype == WLQ_DTYPE_BF16) return dispatch<__nv_bfloat16>(p, row_tiles, cs, stream);
-    return dispatch<__half>(p, row_tiles, cs, stream);
+    while (cs < 8 && (int64_t)ctas * cs < 4LL * sms && p.kchunks >= 2 * (cs + 1)) ++cs;
+    p.chunks_per_rank = (p.kchunks + cs - 1) / cs;
+    p.x_stride = p.chunks_per_rank * kChunk + 8;
+    // stage the rank's activations in shared memory when they are small
+    // (4 CTAs per SM keep fitting); larger slices are read through L1
+    const bool xsmem = (int64_t)a.M * p.x_stride * 2 <= 32 * 1024;
+    if (a.dtype == WLQ_DTYPE_BF16) return dispatch<__nv_bfloat16>(p, a.lut_prepacked, xvec, xsmem, ctas, cs, stream);
+    return dispatch<__half>(p, a.lut_prepacked, xvec, xsmem, ctas, cs, stream);
 }
 
 }  // namespace wlq

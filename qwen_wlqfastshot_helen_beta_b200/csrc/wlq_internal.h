@@ -35,10 +35,15 @@ struct LinearArgs {
     int chunk_m;             // outlier chunk width (512 for 4-bit)
     int ncsr;                // outlier chunks per row
     int dtype;               // WLQ_DTYPE_*
+    bool lut_prepacked;      // WLQ_LUT_PREPACKED codebooks
 };
 
 int launch_gemv(const LinearArgs& a, cudaStream_t stream);
 int launch_gemm(const LinearArgs& a, cudaStream_t stream);
+int launch_prepack_outliers(const uint32_t* q, const uint16_t* lut, const int32_t* off, const uint16_t* ccols,
+                            const uint8_t* cvals, int N, int K, int wpr, int group_size, int goff, int ngroups,
+                            int chunk_m, int ncsr, int dtype, uint16_t* gcols, float* delta, cudaStream_t stream);
+int launch_prepack_lut(const uint16_t* in, uint32_t* out, int64_t n, int dtype, cudaStream_t stream);
 int launch_dequant(const uint32_t* q, const uint16_t* lut, uint16_t* W, const int32_t* off,
                    const uint16_t* ccols, const uint8_t* cvals, int N, int K, int bits, int wpr,
                    int group_size, int group_offset, int ngroups, int chunk_m, int ncsr,

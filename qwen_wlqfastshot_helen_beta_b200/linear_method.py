@@ -221,6 +221,7 @@ class WLQLinearMethod(LinearMethodBase):
         layer.output_partition_sizes = list(output_partition_sizes)
         layer.N = sum(output_partition_sizes)
         layer.K = input_size_per_partition
+        layer.wlq_act_dtype = params_dtype if params_dtype in (torch.float16, torch.bfloat16) else torch.float16
         fp8_t = getattr(torch, "float8_e5m2", torch.uint8)
         specs = [("weight", torch.float16), ("q_packed", torch.int32), ("lut_c", torch.float16),
                  ("bits", torch.int32), ("orig_shape", torch.int32), ("is_quantized", torch.uint8),
@@ -362,6 +363,16 @@ class WLQLinearMethod(LinearMethodBase):
         layer.chunk_offsets = offsets.to(device)
         layer.chunk_cols = cols.to(device)
         layer.chunk_vals = vals.to(device)
+        # codebooks prepacked once for the model's activation dtype (the kernels
+        # then use them without conversion); lut_c keeps the reference layout
+        act_dt = getattr(layer, "wlq_act_dtype", torch.float16)
+        layer.lut_packed = _C.prepack_lut(layer.lut_c, act_dt)
+        layer.lut_packed_dtype = act_dt
+        layer.cols_packed = layer.delta_packed = None
+        if device.type == "cuda" and cols.numel() > 0:
+            layer.cols_packed, layer.delta_packed = _C.prepack_outliers(
+                layer.q_packed_aligned, layer.lut_c, layer.chunk_offsets, layer.chunk_cols, layer.chunk_vals,
+                layer.N, layer.K, bits, act_dt, G, goff)
         layer.has_dora = has_dora
         layer.lora_A_f16 = lora_A_f16 if has_dora else None
         layer.lora_B = lora_B_f16
@@ -458,17 +469,26 @@ class WLQLinearMethod(LinearMethodBase):
         G = getattr(layer, "lut_group_size", 0)
         goff = getattr(layer, "lut_group_offset", 0)
         scale = getattr(layer, "lora_scale", 1.0)
+        cols, vals = layer.chunk_cols, layer.chunk_vals
+        if getattr(layer, "lut_packed", None) is not None and layer.lut_packed_dtype == x2.dtype and \
+                (cols.numel() == 0 or getattr(layer, "cols_packed", None) is not None):
+            lut, fmt = layer.lut_packed, 1
+            if cols.numel() > 0:
+                cols, vals = layer.cols_packed, layer.delta_packed
+        else:
+            lut, fmt = layer.lut_c, 0
         lora_h = None
         if has_dora and layer.lora_A_f16 is not None:
             lora_h = F.linear(x2, self._lora_A(layer, x2.dtype)).float()
         if M == 1:
-            torch.ops.wlq_fastShot.gemv(layer.q_packed_aligned, layer.lut_c, x2.squeeze(0), out.squeeze(0), layer.N,
-                                        layer.K, bits, layer.chunk_offsets, layer.chunk_cols, layer.chunk_vals,
-                                        lora_B, None if lora_h is None else lora_h.squeeze(0), gamma, scale, G, goff)
+            torch.ops.wlq_fastShot.gemv(layer.q_packed_aligned, lut, x2.squeeze(0), out.squeeze(0), layer.N,
+                                        layer.K, bits, layer.chunk_offsets, cols, vals,
+                                        lora_B, None if lora_h is None else lora_h.squeeze(0), gamma, scale, G, goff,
+                                        fmt)
         else:
-            torch.ops.wlq_fastShot.gemm(x2, layer.q_packed_aligned, layer.lut_c, out, layer.N, layer.K, bits,
-                                        layer.words_per_row, layer.chunk_offsets, layer.chunk_cols,
-                                        layer.chunk_vals, lora_h, lora_B, gamma, scale, G, goff)
+            torch.ops.wlq_fastShot.gemm(x2, layer.q_packed_aligned, lut, out, layer.N, layer.K, bits,
+                                        layer.words_per_row, layer.chunk_offsets, cols, vals, lora_h, lora_B,
+                                        gamma, scale, G, goff, fmt)
         if out.dtype != orig_dtype:
             out = out.to(orig_dtype)
         if bias is not None:

@@ -45,6 +45,26 @@ class SyntheticLayer:
     dora_gamma: Optional[torch.Tensor]
     lora_scale: float
     nnz: int
+    lut_packed: Optional[torch.Tensor] = None   # WLQ_LUT_PREPACKED layout for packed_dtype
+    cols_packed: Optional[torch.Tensor] = None
+    delta_packed: Optional[torch.Tensor] = None
+    packed_dtype: Optional[torch.dtype] = None
+
+    def prepack(self, act_dtype: torch.dtype) -> "SyntheticLayer":
+        self.lut_packed = _C.prepack_lut(self.lut_c.contiguous(), act_dtype)
+        if self.chunk_cols is not None and self.q_packed.is_cuda:
+            self.cols_packed, self.delta_packed = _C.prepack_outliers(
+                self.q_packed, self.lut_c, self.chunk_offsets, self.chunk_cols, self.chunk_vals, self.N, self.K, 4,
+                act_dtype, self.group_size, self.group_offset)
+        self.packed_dtype = act_dtype
+        return self
+
+    def operands_for(self, act_dtype: torch.dtype):
+        """(codebooks, outlier cols, outlier vals, lut_format) for act_dtype."""
+        if self.lut_packed is not None and self.packed_dtype == act_dtype and \
+                (self.chunk_cols is None or self.cols_packed is not None):
+            return self.lut_packed, self.cols_packed, self.delta_packed, 1
+        return self.lut_c, self.chunk_cols, self.chunk_vals, 0
 
     @property
     def r(self) -> int:
@@ -178,9 +198,10 @@ def forward(layer: SyntheticLayer, x: torch.Tensor, out: Optional[torch.Tensor] 
         out = torch.empty((M, layer.N), dtype=x.dtype, device=x.device)
     if h is None:
         h = lora_h(layer, x)
-    _C.gemm_forward(x, layer.q_packed, layer.lut_c, out, layer.N, layer.K, 4, layer.words_per_row,
-                    layer.chunk_offsets, layer.chunk_cols, layer.chunk_vals, h, layer.lora_B, layer.dora_gamma,
-                    layer.lora_scale, layer.group_size, layer.group_offset)
+    lut, cols, vals, fmt = layer.operands_for(x.dtype)
+    _C.gemm_forward(x, layer.q_packed, lut, out, layer.N, layer.K, 4, layer.words_per_row,
+                    layer.chunk_offsets, cols, vals, h, layer.lora_B, layer.dora_gamma,
+                    layer.lora_scale, layer.group_size, layer.group_offset, fmt)
     return out
 
 

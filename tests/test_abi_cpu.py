@@ -38,26 +38,53 @@ def test_argument_validation_without_gpu():
     import ctypes
     from qwen_wlqfastshot_helen_beta_b200._lib import lib
     p = ctypes.c_void_p(16)
+    # argument order: ..., r, M, N, K, bits, words_per_row, group_size, group_offset, lut_format, act_dtype, stream
     # bits != 4 is rejected before any device call
-    rc = lib.wlq_gemv(p, p, p, p, None, None, None, None, None, None, 1.0, 0, 1, 8, 64, 3, 4, 0, 0, 0, None)
+    rc = lib.wlq_gemv(p, p, p, p, None, None, None, None, None, None, 1.0, 0, 1, 8, 64, 3, 4, 0, 0, 0, 0, None)
     assert rc == 2 and b"4-bit" in lib.wlq_last_error()
     # wrong words_per_row
-    rc = lib.wlq_gemm(p, p, p, p, None, None, None, None, None, None, 1.0, 0, 32, 8, 64, 4, 7, 0, 0, 0, None)
+    rc = lib.wlq_gemm(p, p, p, p, None, None, None, None, None, None, 1.0, 0, 32, 8, 64, 4, 7, 0, 0, 0, 0, None)
     assert rc == 1 and b"words_per_row" in lib.wlq_last_error()
-    # unknown dtype
-    rc = lib.wlq_gemm(p, p, p, p, None, None, None, None, None, None, 1.0, 0, 32, 8, 64, 4, 8, 0, 0, 7, None)
+    # unknown dtype / codebook format
+    rc = lib.wlq_gemm(p, p, p, p, None, None, None, None, None, None, 1.0, 0, 32, 8, 64, 4, 8, 0, 0, 0, 7, None)
     assert rc == 2
+    rc = lib.wlq_gemm(p, p, p, p, None, None, None, None, None, None, 1.0, 0, 32, 8, 64, 4, 8, 0, 0, 5, 0, None)
+    assert rc == 1 and b"lut_format" in lib.wlq_last_error()
     # misaligned q
     rc = lib.wlq_gemv(ctypes.c_void_p(18), p, p, p, None, None, None, None, None, None, 1.0, 0, 1, 8, 64, 4, 8, 0, 0,
-                      0, None)
+                      0, 0, None)
     assert rc == 3
     # empty problem is a no-op success
     assert lib.wlq_gemv(None, None, None, None, None, None, None, None, None, None, 1.0, 0, 0, 0, 0, 4, 0, 0, 0, 0,
-                        None) == 0
+                        0, None) == 0
     assert lib.wlq_init_workspaces(-1, 4, 0) == 1
     assert lib.wlq_init_workspaces(4096, 4096, 0) == 0
     assert lib.wlq_words_per_row(3584, 4) == 448 and lib.wlq_words_per_row(18944, 4) == 2368
     assert lib.wlq_words_per_row(37, 4) == 8 and lib.wlq_words_per_row(50, 3) == 8
+    # prepacking: overlapping buffers and bad dtypes are refused
+    buf = ctypes.create_string_buffer(64 + 16)
+    base = (ctypes.addressof(buf) + 15) // 16 * 16
+    assert lib.wlq_prepack_lut(ctypes.c_void_p(base), ctypes.c_void_p(base), 1, 0, None) == 1
+    assert lib.wlq_prepack_lut_host(ctypes.c_void_p(base), ctypes.c_void_p(base + 32), 1, 9) == 1
+
+
+def test_prepack_host_layout():
+    """Prepacked codebook = entries in the MMA type, low bytes then high bytes."""
+    from qwen_wlqfastshot_helen_beta_b200 import _C
+    from oracle import oracle as O
+    rng = np.random.default_rng(8)
+    lut = (rng.standard_normal((5, 3, 16)) * 0.03).astype(np.float16)
+    lut[0, 0, :4] = np.array([0.0, -0.0, 6e-5, 65504], np.float16)
+    for dt in (torch.float16, torch.bfloat16):
+        pk = _C.prepack_lut(torch.from_numpy(lut), dt).numpy().view(np.uint8).reshape(-1, 32)
+        flat = lut.reshape(-1, 16)
+        if dt == torch.float16:
+            vals = flat.view(np.uint16)
+        else:
+            vals = np.array([[O.lib().orc_f32_to_bf16(float(v)) for v in row] for row in flat.astype(np.float32)],
+                            np.uint16)
+        assert np.array_equal(pk[:, :16], (vals & 0xFF).astype(np.uint8))
+        assert np.array_equal(pk[:, 16:], (vals >> 8).astype(np.uint8))
 
 
 def test_codecs_repack_against_golden(golden_codecs):

@@ -44,15 +44,21 @@ def dev_layer(L):
     return t
 
 
-def run_ours(L, T, x, h, gemv=False):
+def run_ours(L, T, x, h, gemv=False, fmt=0):
     M = x.shape[0]
     out = torch.full((M, L.N), float("nan"), dtype=x.dtype, device="cuda")
+    lut, cols, vals = T["lut"], T["cols"], T["vals"]
+    if fmt == 1:
+        lut = C().prepack_lut(T["lut"], x.dtype)
+        if cols is not None:
+            cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], L.N, L.K, 4, x.dtype,
+                                              L.G, L.goff)
     if gemv:
-        C().gemv_forward(T["q"], T["lut"], x, out, L.N, L.K, 4, T["off"], T["cols"], T["vals"], T["B"], h,
-                         T["gamma"], L.scale, L.G, L.goff)
+        C().gemv_forward(T["q"], lut, x, out, L.N, L.K, 4, T["off"], cols, vals, T["B"], h,
+                         T["gamma"], L.scale, L.G, L.goff, fmt)
     else:
-        C().gemm_forward(x, T["q"], T["lut"], out, L.N, L.K, 4, L.wpr, T["off"], T["cols"], T["vals"], h, T["B"],
-                         T["gamma"], L.scale, L.G, L.goff)
+        C().gemm_forward(x, T["q"], lut, out, L.N, L.K, 4, L.wpr, T["off"], cols, vals, h, T["B"],
+                         T["gamma"], L.scale, L.G, L.goff, fmt)
     torch.cuda.synchronize()
     return out
 
@@ -119,11 +125,15 @@ def test_gemv_matches_oracle(case, dtype):
     T = dev_layer(L)
     for M in (1, 2, 3, 7, 8, 9, 15, 16):
         x, h = inputs(rng, L, M, dtype)
-        y = run_ours(L, T, x, h, gemv=(M == 1))
         ref = reference_output(L, x.float().cpu().numpy(), None if h is None else h.cpu().numpy())
-        e = rel_err(y.float().cpu().numpy(), ref)
-        assert e <= TOL[dtype], (M, e)
-        assert torch.isfinite(y).all()
+        ys = []
+        for fmt in (0, 1):  # reference fp16 codebooks, prepacked codebooks
+            y = run_ours(L, T, x, h, gemv=(M == 1), fmt=fmt)
+            e = rel_err(y.float().cpu().numpy(), ref)
+            assert e <= TOL[dtype], (M, fmt, e)
+            assert torch.isfinite(y).all()
+            ys.append(y)
+        assert torch.equal(ys[0], ys[1])  # same arithmetic either way
 
 
 def test_gemv_outlier_edges():
@@ -143,9 +153,10 @@ def test_gemv_outlier_edges():
     for M in (1, 4, 16):
         for dtype in (torch.float16, torch.bfloat16):
             x, h = inputs(rng, L, M, dtype)
-            y = run_ours(L, T, x, h)
             ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
-            assert rel_err(y.float().cpu().numpy(), ref) <= TOL[dtype], (M, dtype)
+            for fmt in (0, 1):
+                y = run_ours(L, T, x, h, fmt=fmt)
+                assert rel_err(y.float().cpu().numpy(), ref) <= TOL[dtype], (M, dtype, fmt)
 
 
 # ------------------------------------------------- the reference's kernels
@@ -303,6 +314,6 @@ def test_errors_are_raised():
         C().gemm_forward(x.float(), T["q"], T["lut"], out.float(), 32, 256, 4, L.wpr, None, None, None)
     with pytest.raises(RuntimeError, match="lut_c"):
         C().gemm_forward(x, T["q"], T["lut"][:16], out, 32, 256, 4, L.wpr, None, None, None)
-    with pytest.raises(RuntimeError, match="multiples of 32"):
+    with pytest.raises(RuntimeError, match="multiple of 32"):
         C().gemm_forward(x, T["q"], torch.zeros(32 * 3 * 16, dtype=torch.float16, device="cuda"), out, 32, 256, 4,
                          L.wpr, None, None, None, lut_group_size=128, lut_group_offset=16)
