@@ -17,11 +17,14 @@
 //    reference fp16 layout is accepted too and rebuilt per lane;
 //  * the A fragment's k order is free (the same permutation is applied to x):
 //    lane (g, t) owns rows g and g+8 and the 32 consecutive columns
-//    [32t, 32t+32) of every 128-wide chunk, so it reads 16 contiguous bytes of
-//    each of its rows per chunk with one 128-bit load; DEPTH chunks of index
-//    words and the next chunk's codebooks are in flight per lane;
+//    [32t, 32t+32) of every 128-wide chunk, i.e. 16 contiguous bytes of each
+//    of its rows per chunk;
+//  * index words and codebooks stream through a per-warp shared-memory ring
+//    filled with cp.async (kStages chunks in flight): prefetches hold no
+//    registers or scoreboards, and a chunk is read with one 128-bit shared
+//    load per row;
 //  * the CTA stages its K range of the activations in shared memory once
-//    (cp.async), so the B fragments are short-latency shared loads;
+//    (cp.async) when it fits, so the B fragments are short-latency loads;
 //  * each warp owns a 16-row tile; K is split only across the CTAs of a
 //    thread-block cluster, whose partial tiles meet in distributed shared
 //    memory: no global workspace, no second launch.
@@ -58,6 +61,7 @@ struct GemvParams {
     int kchunks;           // ceil(K / 128)
     int chunks_per_rank;   // K split across the cluster
     int x_stride;          // shared-memory row stride of staged activations (elements)
+    int x_bytes;           // bytes of dynamic shared memory before the ring (staged activations)
     uint32_t mul16, mul31; // 1<<16 and 1<<31, runtime values so mul.hi stays a multiply
 };
 
@@ -94,13 +98,7 @@ __device__ __forceinline__ void lookup4(const LutPlanes& p, uint32_t sel, uint32
 // Codebook planes of one (row, group): prepacked (8 words: lo[4], hi[4]) or
 // the reference's 16 fp16 entries, converted and permuted here.
 template <typename T, bool PREPACKED>
-__device__ __forceinline__ void load_planes(const uint16_t* __restrict__ lut, int64_t entry, bool valid,
-                                            LutPlanes& P) {
-    uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
-    if (valid) {  // streamed: the 4 lanes sharing a codebook read it in one request
-        a = ldg_stream_v4(lut + entry * 16);
-        b = ldg_stream_v4(lut + entry * 16 + 8);
-    }
+__device__ __forceinline__ void planes_from_words(const uint4 a, const uint4 b, LutPlanes& P) {
     if (PREPACKED) {
         P.lo[0] = a.x; P.lo[1] = a.y; P.lo[2] = a.z; P.lo[3] = a.w;
         P.hi[0] = b.x; P.hi[1] = b.y; P.hi[2] = b.z; P.hi[3] = b.w;
@@ -116,6 +114,22 @@ __device__ __forceinline__ void load_planes(const uint16_t* __restrict__ lut, in
         }
     }
     make_planes(e, P);
+}
+
+template <typename T, bool PREPACKED>
+__device__ __forceinline__ void load_planes(const uint16_t* __restrict__ lut, int64_t entry, bool valid,
+                                            LutPlanes& P) {
+    uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
+    if (valid) {  // the 4 lanes sharing a codebook read it in one request
+        a = ldg_stream_v4(lut + entry * 16);
+        b = ldg_stream_v4(lut + entry * 16 + 8);
+    }
+    planes_from_words<T, PREPACKED>(a, b, P);
+}
+
+template <typename T, bool PREPACKED>
+__device__ __forceinline__ void planes_from_smem(uint32_t addr, LutPlanes& P) {
+    planes_from_words<T, PREPACKED>(lds128(addr), lds128(addr + 16), P);
 }
 
 // Codebook value of symbol q of one (row, group) as the MMA saw it.
@@ -152,11 +166,25 @@ __device__ __forceinline__ void stage_x(uint16_t* xs, const T* __restrict__ x, i
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-template <typename T, int NT, bool GROUPED, bool PREPACKED, bool XVEC, bool XSMEM, int DEPTH>
+// Per-warp shared-memory ring of S stages, filled by cp.async (no register
+// scoreboards held by prefetches).  A stage holds one 128-column chunk: the
+// index words of the warp's 16 rows (16 x 64 B) and, with per-group
+// codebooks, NSLOT codebooks per row (16 x NSLOT x 32 B), slot s holding group
+// g0 + s where g0 is the group of the chunk's first column.
+template <int NSLOT>
+struct Ring {
+    static constexpr int kIdxBytes = kRowsPerTile * 64;
+    static constexpr int kPlaneBytes = kRowsPerTile * NSLOT * 32;
+    static constexpr int kStageBytes = kIdxBytes + kPlaneBytes;
+};
+
+template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int S>
 __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p) {
+    constexpr bool GROUPED = NSLOT > 0;
     constexpr int MT = 8 * NT;
-    extern __shared__ __align__(16) uint16_t xs[];  // [M][x_stride] activations of this rank's K range
-    static_assert(DEPTH % 2 == 0, "the codebook ring alternates slots with chunk parity");
+    using R = Ring<NSLOT>;
+    static_assert(S >= 2, "ring needs two stages");
+    extern __shared__ __align__(128) uint8_t smem[];  // [x stage (XSMEM)][kWarps][S] ring stages
     __shared__ float part[kWarps][kRowsPerTile][MT];  // per-warp partial tile
 
     const int warp = threadIdx.x >> 5;
@@ -165,27 +193,57 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
     const int t = lane & 3;
     const int tile_row0 = (blockIdx.x * kWarps + warp) * kRowsPerTile;
     const int row0 = tile_row0 + g;
-    const int row1 = row0 + 8;
     const bool v0 = row0 < p.N;
-    const bool v1 = row1 < p.N;
-    const uint32_t* q0 = p.q + (int64_t)(v0 ? row0 : 0) * p.wpr;
-    const uint32_t* q1 = p.q + (int64_t)(v1 ? row1 : 0) * p.wpr;
+    const bool v1 = row0 + 8 < p.N;
     const T* x = reinterpret_cast<const T*>(p.x);
     const uint32_t m16 = p.mul16, m31 = p.mul31;
-    const int64_t cb0 = (int64_t)(v0 ? row0 : 0) * p.ngroups;  // codebook entry base of each row
-    const int64_t cb1 = (int64_t)(v1 ? row1 : 0) * p.ngroups;
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem);  // [M][x_stride] activations of this rank's K range
+    const uint32_t ring = smem_u32(smem + p.x_bytes) + (uint32_t)(warp * S * R::kStageBytes);
 
     const int c_begin = blockIdx.y * p.chunks_per_rank;
     const int c_end = min(p.kchunks, c_begin + p.chunks_per_rank);
 
-    uint4 wa[DEPTH], wb[DEPTH];
+    // codebook group of a column (clamped: columns past K meet zero activations)
+    auto group_at = [&](int col) { return min((col + p.goff) >> p.log2G, p.ngroups - 1); };
+
+    // chunk c into ring stage st; one commit group per lane per chunk, empty
+    // past the rank's range
+    auto issue = [&](int c, int st) {
+        if (c < c_end) {
+            const uint32_t base = ring + (uint32_t)(st * R::kStageBytes);
 #pragma unroll
-    for (int j = 0; j < DEPTH; ++j) {
-        const int c = c_begin + j;
-        const int wi = c * (kChunk / 8) + 4 * t;
-        const bool in = c < c_end && wi < p.wpr;
-        wa[j] = (v0 && in) ? ldg_stream_v4(q0 + wi) : make_uint4(0u, 0u, 0u, 0u);
-        wb[j] = (v1 && in) ? ldg_stream_v4(q1 + wi) : make_uint4(0u, 0u, 0u, 0u);
+            for (int i = 0; i < 2; ++i) {
+                const int pc = lane + 32 * i;
+                const int r = pc >> 2, q4 = pc & 3;
+                const int row = tile_row0 + r;
+                const int wi = c * (kChunk / 8) + 4 * q4;
+                const bool ok = row < p.N && wi < p.wpr;
+                cp_async16(base + r * 64 + q4 * 16, p.q + (ok ? (int64_t)row * p.wpr + wi : 0), ok);
+            }
+            if constexpr (GROUPED) {
+                const int g0 = group_at(c * kChunk);
+                const int used = group_at(c * kChunk + kChunk - 1) - g0 + 1;
+#pragma unroll
+                for (int i = 0; i < NSLOT; ++i) {
+                    const int pc = lane + 32 * i;
+                    const int r = pc / (2 * NSLOT), s = (pc >> 1) % NSLOT, half = pc & 1;
+                    const int row = tile_row0 + r;
+                    const bool ok = row < p.N && s < used;
+                    cp_async16(base + R::kIdxBytes + (r * NSLOT + s) * 32 + half * 16,
+                               p.lut + (ok ? ((int64_t)row * p.ngroups + g0 + s) * 16 + 8 * half : 0), ok);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int j = 0; j < S - 1; ++j) issue(c_begin + j, j);
+
+    // per-row codebooks (no grouping) stay in registers for the whole K range
+    LutPlanes PR0, PR1;
+    if (!GROUPED) {
+        load_planes<T, PREPACKED>(p.lut, row0, v0, PR0);
+        load_planes<T, PREPACKED>(p.lut, row0 + 8, v1, PR1);
     }
 
     float acc[NT][4];
@@ -194,8 +252,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
 
-    // this rank's activations into shared memory (index words already in flight)
-    // (XSMEM) or read them from L1 when the slice is too large to stage
+    // this rank's activations into shared memory (XSMEM), or read through L1
+    // when the slice is too large to stage
     const int kb0 = c_begin * kChunk;
     if (XSMEM) {
         stage_x<T, XVEC>(xs, x, p.M, p.K, kb0, p.chunks_per_rank * kChunk, p.x_stride);
@@ -211,33 +269,24 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
                         : reinterpret_cast<const uint16_t*>(x) + (int64_t)tok * p.K + kb0 + 32 * t;
     }
 
-    // codebook of this lane's 32 columns of chunk c (lanes past K are clamped:
-    // they multiply zero activations)
-    auto group_of = [&](int c) { return min((c * kChunk + 32 * t + p.goff) >> p.log2G, p.ngroups - 1); };
-    LutPlanes PL[2][2];  // [slot][row0/row1]
-    if (!GROUPED) {
-        load_planes<T, PREPACKED>(p.lut, cb0, v0, PL[0][0]);
-        load_planes<T, PREPACKED>(p.lut, cb1, v1, PL[0][1]);
-    } else if (c_begin < c_end) {
-        const int gg = group_of(c_begin);
-        load_planes<T, PREPACKED>(p.lut, cb0 + gg, v0, PL[0][0]);
-        load_planes<T, PREPACKED>(p.lut, cb1 + gg, v1, PL[0][1]);
-    }
-
-    // activations (shared memory) run one k-step pair ahead of their use
+    // activations run one k-step pair ahead of their use
     auto lds_x8 = [&](int tt, int off) -> uint4 {
         if (!tok_ok[tt]) return make_uint4(0u, 0u, 0u, 0u);
-        if (XSMEM) return *reinterpret_cast<const uint4*>(xrow[tt] + off);
         const int k = kb0 + 32 * t + off;  // global column of this 8-wide piece
-        if (XVEC) return k + 8 <= p.K ? ldg_keep_v4(xrow[tt] + off) : make_uint4(0u, 0u, 0u, 0u);
-        uint32_t w[4];
+        if constexpr (XSMEM) {
+            return *reinterpret_cast<const uint4*>(xrow[tt] + off);
+        } else if constexpr (XVEC) {
+            return k + 8 <= p.K ? ldg_keep_v4(xrow[tt] + off) : make_uint4(0u, 0u, 0u, 0u);
+        } else {
+            uint32_t w[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t lo = k + 2 * j < p.K ? (uint32_t)__ldg(xrow[tt] + off + 2 * j) : 0u;
-            const uint32_t hi = k + 2 * j + 1 < p.K ? (uint32_t)__ldg(xrow[tt] + off + 2 * j + 1) : 0u;
-            w[j] = lo | (hi << 16);
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t lo = k + 2 * j < p.K ? (uint32_t)__ldg(xrow[tt] + off + 2 * j) : 0u;
+                const uint32_t hi = k + 2 * j + 1 < p.K ? (uint32_t)__ldg(xrow[tt] + off + 2 * j + 1) : 0u;
+                w[j] = lo | (hi << 16);
+            }
+            return make_uint4(w[0], w[1], w[2], w[3]);
         }
-        return make_uint4(w[0], w[1], w[2], w[3]);
     };
     auto x_at = [&](int m, int col) -> float {  // activation of token m at global column col
         return XSMEM ? ActTraits<T>::bits_to_f32(xs[m * p.x_stride + col - kb0])
@@ -247,62 +296,60 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt) xnext[tt] = c_begin < c_end ? lds_x8(tt, 0) : make_uint4(0u, 0u, 0u, 0u);
 
-    for (int cb = c_begin; cb < c_end; cb += DEPTH) {
+    int st = 0;
+    for (int c = c_begin; c < c_end; ++c) {
+        cp_async_wait<S - 2>();  // this lane's copies of chunk c have landed
+        __syncwarp();            // ... and every lane's; the previous stage is free
+        issue(c + S - 1, st == 0 ? S - 1 : st - 1);
+        const uint32_t base = ring + (uint32_t)(st * R::kStageBytes);
+        st = st + 1 == S ? 0 : st + 1;
+        const uint4 w0 = lds128(base + g * 64 + 16 * t);
+        const uint4 w1 = lds128(base + (g + 8) * 64 + 16 * t);
+        LutPlanes P0, P1;
+        if (GROUPED) {
+            const int s = group_at(c * kChunk + 32 * t) - group_at(c * kChunk);
+            const uint32_t pb = base + R::kIdxBytes + s * 32;
+            planes_from_smem<T, PREPACKED>(pb + g * (NSLOT * 32), P0);
+            planes_from_smem<T, PREPACKED>(pb + (g + 8) * (NSLOT * 32), P1);
+        } else {
+            P0 = PR0;
+            P1 = PR1;
+        }
+        const uint32_t ra[4] = {w0.x, w0.y, w0.z, w0.w};
+        const uint32_t rb[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int j = 0; j < DEPTH; ++j) {
-            const int c = cb + j;
-            if (c >= c_end) break;
-            const int slot = GROUPED ? (j & 1) : 0;
-            const uint4 w0 = wa[j], w1 = wb[j];
-            {  // refill this slot with chunk c + DEPTH
-                const int cn = c + DEPTH;
-                const int wi = cn * (kChunk / 8) + 4 * t;
-                const bool in = cn < c_end && wi < p.wpr;
-                wa[j] = (v0 && in) ? ldg_stream_v4(q0 + wi) : make_uint4(0u, 0u, 0u, 0u);
-                wb[j] = (v1 && in) ? ldg_stream_v4(q1 + wi) : make_uint4(0u, 0u, 0u, 0u);
-            }
-            if (GROUPED && c + 1 < c_end) {  // next chunk's codebooks into the other slot
-                const int gg = group_of(c + 1);
-                load_planes<T, PREPACKED>(p.lut, cb0 + gg, v0, PL[slot ^ 1][0]);
-                load_planes<T, PREPACKED>(p.lut, cb1 + gg, v1, PL[slot ^ 1][1]);
-            }
-            const uint32_t ra[4] = {w0.x, w0.y, w0.z, w0.w};
-            const uint32_t rb[4] = {w1.x, w1.y, w1.z, w1.w};
+        for (int ws = 0; ws < 4; ++ws) {
+            uint4 xv[NT];
 #pragma unroll
-            for (int ws = 0; ws < 4; ++ws) {
-                uint4 xv[NT];
+            for (int tt = 0; tt < NT; ++tt) {
+                xv[tt] = xnext[tt];
+                // next pair: this chunk's ws+1, or the next chunk's first
+                const int kn = (c - c_begin) * kChunk + (ws < 3 ? 8 * (ws + 1) : kChunk);
+                if (ws < 3 || c + 1 < c_end) xnext[tt] = lds_x8(tt, kn);
+            }
+            const uint32_t sa = ra[ws] & 0x77777777u;
+            const uint32_t ca = lop_and_or(mulhi(ra[ws], m31), 0x44444444u, 0x32103210u);
+            const uint32_t sb = rb[ws] & 0x77777777u;
+            const uint32_t cb2 = lop_and_or(mulhi(rb[ws], m31), 0x44444444u, 0x32103210u);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t a[4];
+                if (h == 0) {
+                    lookup4(P0, sa, ca, a[0], a[2]);
+                    lookup4(P1, sb, cb2, a[1], a[3]);
+                } else {
+                    lookup4(P0, mulhi(sa, m16), mulhi(ca, m16), a[0], a[2]);
+                    lookup4(P1, mulhi(sb, m16), mulhi(cb2, m16), a[1], a[3]);
+                }
 #pragma unroll
                 for (int tt = 0; tt < NT; ++tt) {
-                    xv[tt] = xnext[tt];
-                    // next pair: this chunk's ws+1, or the next chunk's first
-                    const int kn = (c - c_begin) * kChunk + (ws < 3 ? 8 * (ws + 1) : kChunk);
-                    if (ws < 3 || c + 1 < c_end) xnext[tt] = lds_x8(tt, kn);
-                }
-                const uint32_t sa = ra[ws] & 0x77777777u;
-                const uint32_t ca = lop_and_or(mulhi(ra[ws], m31), 0x44444444u, 0x32103210u);
-                const uint32_t sb = rb[ws] & 0x77777777u;
-                const uint32_t cb2 = lop_and_or(mulhi(rb[ws], m31), 0x44444444u, 0x32103210u);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t a[4];
-                    if (h == 0) {
-                        lookup4(PL[slot][0], sa, ca, a[0], a[2]);
-                        lookup4(PL[slot][1], sb, cb2, a[1], a[3]);
-                    } else {
-                        lookup4(PL[slot][0], mulhi(sa, m16), mulhi(ca, m16), a[0], a[2]);
-                        lookup4(PL[slot][1], mulhi(sb, m16), mulhi(cb2, m16), a[1], a[3]);
-                    }
-#pragma unroll
-                    for (int tt = 0; tt < NT; ++tt) {
-                        const uint32_t b0 = h ? xv[tt].z : xv[tt].x;
-                        const uint32_t b1 = h ? xv[tt].w : xv[tt].y;
-                        Mma16816<T>::run(acc[tt], a, b0, b1);
-                    }
+                    const uint32_t b0 = h ? xv[tt].z : xv[tt].x;
+                    const uint32_t b1 = h ? xv[tt].w : xv[tt].y;
+                    Mma16816<T>::run(acc[tt], a, b0, b1);
                 }
             }
         }
     }
-
     // publish this warp's partial tile
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt)
@@ -402,16 +449,19 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
     if (clustered) cluster_sync_all();  // keep every rank's tiles alive until rank 0 is done
 }
 
-template <typename T, int NT, bool GROUPED, bool PREPACKED, bool XVEC, bool XSMEM>
+constexpr int kStages = 3;  // measured: 3 >= 4 > 6 (more stages cost occupancy, not latency)
+
+template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM>
 int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream) {
-    constexpr int DEPTH = NT == 1 ? 4 : 2;
+    auto kern = gemv_kernel<T, NT, NSLOT, PREPACKED, XVEC, XSMEM, kStages>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas, (unsigned)cs, 1);
     cfg.blockDim = dim3(kWarps * 32, 1, 1);
-    const size_t smem = XSMEM ? (size_t)p.M * p.x_stride * 2 : 0;
-    if (smem > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(gemv_kernel<T, NT, GROUPED, PREPACKED, XVEC, XSMEM, DEPTH>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = (size_t)p.x_bytes + (size_t)kWarps * kStages * Ring<NSLOT>::kStageBytes;
+    // the default limit covers static + dynamic shared memory up to 48 KB
+    constexpr size_t kStatic = sizeof(float) * kWarps * kRowsPerTile * 8 * NT;
+    if (smem + kStatic > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return check_cuda(e, "gemv_kernel smem attribute");
     }
     cfg.dynamicSmemBytes = smem;
@@ -423,33 +473,42 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = cs > 1 ? 1 : 0;
-    return check_cuda(cudaLaunchKernelEx(&cfg, gemv_kernel<T, NT, GROUPED, PREPACKED, XVEC, XSMEM, DEPTH>, p),
-                      "gemv_kernel launch");
+    return check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "gemv_kernel launch");
 }
 
-template <typename T, int NT, bool GROUPED, bool PREPACKED>
+template <typename T, int NT, int NSLOT, bool PREPACKED>
 int dispatch_x(const GemvParams& p, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
     if (xsmem)
-        return xvec ? launch_variant<T, NT, GROUPED, PREPACKED, true, true>(p, ctas, cs, stream)
-                    : launch_variant<T, NT, GROUPED, PREPACKED, false, true>(p, ctas, cs, stream);
-    return xvec ? launch_variant<T, NT, GROUPED, PREPACKED, true, false>(p, ctas, cs, stream)
-                : launch_variant<T, NT, GROUPED, PREPACKED, false, false>(p, ctas, cs, stream);
+        return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, true>(p, ctas, cs, stream)
+                    : launch_variant<T, NT, NSLOT, PREPACKED, false, true>(p, ctas, cs, stream);
+    return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, false>(p, ctas, cs, stream)
+                : launch_variant<T, NT, NSLOT, PREPACKED, false, false>(p, ctas, cs, stream);
 }
 
-template <typename T, int NT, bool GROUPED>
+template <typename T, int NT, int NSLOT>
 int dispatch_fmt(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
-    return prepacked ? dispatch_x<T, NT, GROUPED, true>(p, xvec, xsmem, ctas, cs, stream)
-                     : dispatch_x<T, NT, GROUPED, false>(p, xvec, xsmem, ctas, cs, stream);
+    return prepacked ? dispatch_x<T, NT, NSLOT, true>(p, xvec, xsmem, ctas, cs, stream)
+                     : dispatch_x<T, NT, NSLOT, false>(p, xvec, xsmem, ctas, cs, stream);
+}
+
+// codebook slots a 128-column chunk needs per row: 1 without grouping
+// (registers, no slot), 2 for groups of >= 128 columns, 4 for 32 and 64
+inline int codebook_slots(int G) { return G == 0 ? 0 : G >= kChunk ? 2 : 4; }
+
+template <typename T, int NT>
+int dispatch_slots(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs,
+                   cudaStream_t stream) {
+    switch (codebook_slots(p.G)) {
+        case 0: return dispatch_fmt<T, NT, 0>(p, prepacked, xvec, xsmem, ctas, cs, stream);
+        case 2: return dispatch_fmt<T, NT, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream);
+        default: return dispatch_fmt<T, NT, 4>(p, prepacked, xvec, xsmem, ctas, cs, stream);
+    }
 }
 
 template <typename T>
 int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
-    const bool grouped = p.G > 0;
-    if (p.M <= 8)
-        return grouped ? dispatch_fmt<T, 1, true>(p, prepacked, xvec, xsmem, ctas, cs, stream)
-                       : dispatch_fmt<T, 1, false>(p, prepacked, xvec, xsmem, ctas, cs, stream);
-    return grouped ? dispatch_fmt<T, 2, true>(p, prepacked, xvec, xsmem, ctas, cs, stream)
-                   : dispatch_fmt<T, 2, false>(p, prepacked, xvec, xsmem, ctas, cs, stream);
+    return p.M <= 8 ? dispatch_slots<T, 1>(p, prepacked, xvec, xsmem, ctas, cs, stream)
+                    : dispatch_slots<T, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream);
 }
 
 }  // namespace
@@ -486,9 +545,13 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     while (cs < 8 && (int64_t)ctas * cs < 4LL * sms && p.kchunks >= 2 * (cs + 1)) ++cs;
     p.chunks_per_rank = (p.kchunks + cs - 1) / cs;
     p.x_stride = p.chunks_per_rank * kChunk + 8;
-    // stage the rank's activations in shared memory when they are small
-    // (4 CTAs per SM keep fitting); larger slices are read through L1
-    const bool xsmem = (int64_t)a.M * p.x_stride * 2 <= 32 * 1024;
+    // stage the rank's activations in shared memory when 4 CTAs per SM still
+    // fit beside the rings; larger slices are read through L1
+    const int slots = codebook_slots(p.G);
+    const int ring_bytes = kWarps * kStages * (kRowsPerTile * 64 + kRowsPerTile * slots * 32);
+    const int64_t x_bytes = ((int64_t)a.M * p.x_stride * 2 + 127) / 128 * 128;
+    const bool xsmem = x_bytes + ring_bytes <= 48 * 1024;
+    p.x_bytes = xsmem ? (int)x_bytes : 0;
     if (a.dtype == WLQ_DTYPE_BF16) return dispatch<__nv_bfloat16>(p, a.lut_prepacked, xvec, xsmem, ctas, cs, stream);
     return dispatch<__half>(p, a.lut_prepacked, xvec, xsmem, ctas, cs, stream);
 }
