@@ -130,6 +130,14 @@ WLQ_API int wlq_dequant(const int32_t* q_packed, const void* lut_c, void* W_out,
  * the kernels of this library need no workspace, so this only validates. */
 WLQ_API int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device);
 
+/* Device error word of `device`: bit 0 (WLQ_DEVERR_WAIT_TIMEOUT) is set when
+ * a pipeline wait inside a tensor-core GEMM kernel gave up (the kernel then
+ * abandons its tile and its output is undefined).  Synchronous; clears the
+ * word when `clear` is non-zero.  No reference counterpart: the reference
+ * kernels have no bounded waits. */
+#define WLQ_DEVERR_WAIT_TIMEOUT 1u
+WLQ_API int wlq_device_error(int device, unsigned int* flags_out, int clear);
+
 /* ---------------------------------------------------------------- CPU --- */
 /* Load-time codecs (host memory). */
 

@@ -242,6 +242,15 @@ def init_workspaces(max_N, max_K, device):
     check(lib.wlq_init_workspaces(int(max_N), int(max_K), dev.index or 0), "wlq_init_workspaces")
 
 
+def device_error(device=None, clear: bool = True) -> int:
+    """Device error word (bit 0: a bounded pipeline wait in a GEMM kernel
+    gave up, so that call's output is undefined).  Synchronous."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    flags = ctypes.c_uint(0)
+    check(lib.wlq_device_error(dev.index or 0, ctypes.byref(flags), 1 if clear else 0), "wlq_device_error")
+    return int(flags.value)
+
+
 # ----------------------------------------------------------------- codecs ---
 
 def _cpu_i32(t: torch.Tensor) -> torch.Tensor:

@@ -1,6 +1,6 @@
 """ctypes binding of libwlq_b200.so, the package's C ABI (include/wlq_b200.h).
 
-The shared library is built in-tree by ``qwen_wlqfastshot_helen_beta_b200.build``.
+The shared library is built in-tree by ``qwen_wlqfastshot_helen_beta_b200/build.py``.
 There is no fallback: if it is missing, importing this module raises.
 """
 from __future__ import annotations
@@ -35,6 +35,7 @@ SIGNATURES = {
                                     _p]),
     "wlq_dequant": (_i32, [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p]),
     "wlq_init_workspaces": (_i32, [_i64, _i64, _i32]),
+    "wlq_device_error": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint), _i32]),
     "wlq_words_per_row": (_i64, [_i64, _i32]),
     "wlq_repack_q_indices_row_aligned": (_i32, [_p, _i64, _i64, _i64, _i32, _p, _i64, _p64]),
     "wlq_repack_q_indices_slice": (_i32, [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i64, _p, _i64, _p64]),
@@ -50,7 +51,7 @@ SIGNATURES = {
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m qwen_wlqfastshot_helen_beta_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python qwen_wlqfastshot_helen_beta_b200/build.py` "
             "(nvcc for sm_100a); there is no fallback implementation")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():

@@ -1,6 +1,8 @@
 """Build recipe of libwlq_b200.so (sm_100a only), in-tree.
 
-    python -m qwen_wlqfastshot_helen_beta_b200.build [--force] [--verbose]
+    python qwen_wlqfastshot_helen_beta_b200/build.py [--force] [--verbose]
+
+(run as a script: importing the package loads the library built here).
 
 Compiles every ``csrc/*.cu`` with nvcc for ``arch=compute_100a,code=sm_100a``
 and ``csrc/*.cpp`` with g++, then links one shared library next to this file

@@ -237,4 +237,10 @@ int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device) {
     return WLQ_OK;
 }
 
+int wlq_device_error(int device, unsigned int* flags_out, int clear) {
+    g_last_error[0] = '\0';
+    if (!flags_out || device < 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_device_error: bad arguments");
+    return read_device_error(device, flags_out, clear);
+}
+
 }  // extern "C"

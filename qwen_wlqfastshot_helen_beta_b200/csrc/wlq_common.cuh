@@ -116,27 +116,71 @@ __device__ __forceinline__ void make_planes(const uint32_t e[8], LutPlanes& p) {
     }
 }
 
-// Looks up the four indices in the low 16 bits of `sel` (index & 7 per
-// nibble) / `csel` (byte-choose selector per nibble, see lut_selectors) and
-// returns packed pairs (T[q0], T[q1]) and (T[q2], T[q3]).
-__device__ __forceinline__ void lut4(const LutPlanes& p, uint32_t sel, uint32_t csel, uint32_t& o01,
-                                     uint32_t& o23) {
-    const uint32_t la = __byte_perm(p.lo[0], p.lo[1], sel);
-    const uint32_t lb = __byte_perm(p.lo[2], p.lo[3], sel);
-    const uint32_t ha = __byte_perm(p.hi[0], p.hi[1], sel);
-    const uint32_t hb = __byte_perm(p.hi[2], p.hi[3], sel);
-    const uint32_t lo = __byte_perm(la, lb, csel);
-    const uint32_t hi = __byte_perm(ha, hb, csel);
-    o01 = __byte_perm(lo, hi, 0x5140);
-    o23 = __byte_perm(lo, hi, 0x7362);
+// x >> 16 and x >> 1 on the FMA pipe (mul.hi by a runtime power of two).
+__device__ __forceinline__ uint32_t mulhi(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+    return d;
+}
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(m), "r"(o));  // (a & m) | o
+    return d;
 }
 
-// For a word of 8 nibbles: sel keeps the low 3 bits of each nibble (the
-// permute's sign-replicate bit must be clear); csel's nibble i is i (i mod 4)
-// plus 4 when bit 3 of index i is set.
-__device__ __forceinline__ void lut_selectors(uint32_t w, uint32_t& sel, uint32_t& csel) {
-    sel = w & 0x77777777u;
-    csel = ((w >> 1) & 0x44444444u) | 0x32103210u;
+// (T[q0],T[q1]) and (T[q2],T[q3]) for the four indices in the low 16 bits.
+__device__ __forceinline__ void lookup4(const LutPlanes& p, uint32_t sel, uint32_t csel, uint32_t& o01,
+                                        uint32_t& o23) {
+    const uint32_t la = prmt(p.lo[0], p.lo[1], sel);
+    const uint32_t lb = prmt(p.lo[2], p.lo[3], sel);
+    const uint32_t ha = prmt(p.hi[0], p.hi[1], sel);
+    const uint32_t hb = prmt(p.hi[2], p.hi[3], sel);
+    const uint32_t lo = prmt(la, lb, csel);
+    const uint32_t hi = prmt(ha, hb, csel);
+    o01 = prmt(lo, hi, 0x5140u);
+    o23 = prmt(lo, hi, 0x7362u);
+}
+
+// Codebook planes of one (row, group): prepacked (8 words: lo[4], hi[4]) or
+// the reference's 16 fp16 entries, converted and permuted here.
+template <typename T, bool PREPACKED>
+__device__ __forceinline__ void planes_from_words(const uint4 a, const uint4 b, LutPlanes& P) {
+    if (PREPACKED) {
+        P.lo[0] = a.x; P.lo[1] = a.y; P.lo[2] = a.z; P.lo[3] = a.w;
+        P.hi[0] = b.x; P.hi[1] = b.y; P.hi[2] = b.z; P.hi[3] = b.w;
+        return;
+    }
+    uint32_t e[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    if (!ActTraits<T>::kIsF16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&e[i]));
+            const __nv_bfloat162 v = __float22bfloat162_rn(f);
+            e[i] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+    }
+    make_planes(e, P);
+}
+
+template <typename T, bool PREPACKED>
+__device__ __forceinline__ void load_planes(const uint16_t* __restrict__ lut, int64_t entry, bool valid,
+                                            LutPlanes& P) {
+    uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
+    if (valid) {  // the 4 lanes sharing a codebook read it in one request
+        a = ldg_stream_v4(lut + entry * 16);
+        b = ldg_stream_v4(lut + entry * 16 + 8);
+    }
+    planes_from_words<T, PREPACKED>(a, b, P);
+}
+
+template <typename T, bool PREPACKED>
+__device__ __forceinline__ void planes_from_smem(uint32_t addr, LutPlanes& P) {
+    planes_from_words<T, PREPACKED>(lds128(addr), lds128(addr + 16), P);
 }
 
 // ---------------------------------------------------------------------------

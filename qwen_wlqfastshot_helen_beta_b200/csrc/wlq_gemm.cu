@@ -1,9 +1,544 @@
-// Prefill GEMM (M > 16) -- placeholder until the tcgen05 kernel lands.
+// Prefill GEMM for M > 16 token rows over 4-bit LUT-quantised weights, with
+// outlier replacement and the DoRA epilogue fused, on the sm_100a tensor
+// cores (tcgen05, accumulators in TMEM).  Replaces the reference's
+// dequant_patch_metalog + at::mm_out + fused_dora_epilogue sequence
+// (csrc/gemm_kernel.cu:296-526, csrc/vllm_binding.cpp:355-393), which
+// materialises the whole dequantised weight in HBM before a cuBLAS GEMM.
+//
+// One CTA computes a (NACC x 128) x 128 tile of out = gamma * (X W^T + s H B^T):
+//   warp 0      TMA producer: X tiles (64 k x 128 tokens, 128-byte swizzle),
+//               the 128 x 64 index tile and its codebooks, per pipeline stage;
+//   warp 1      allocates TMEM and issues tcgen05.mma from one thread;
+//   warps 2..5  one weight row per thread: LUT lookups in registers (byte
+//               permutes, as in the decode GEMV) written as the K-major
+//               128-byte-swizzled bf16/f16 tile the MMA reads, outlier values
+//               patched in, then the epilogue (TMEM -> gamma -> global).
+// The DoRA low-rank term runs as extra K steps: the dequant warps write
+// s * H (tokens x r) and B (rows x r) into a stage's operand buffers, so it
+// accumulates into the same TMEM tile with no separate epilogue pass.
+// Every mbarrier wait is bounded; a wait that runs out sets the device error
+// word (wlq_device_error) and the CTA winds down, releasing its TMEM.
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
 #include "wlq_common.cuh"
 #include "wlq_internal.h"
+#include "wlq_sm100.cuh"
 
 namespace wlq {
-int launch_gemm(const LinearArgs& a, cudaStream_t) {
-    return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemm: M=%d > 16 needs the tensor-core GEMM, not in this build", a.M);
+
+namespace {
+
+constexpr int kBK = 64;           // k per stage: one 128-byte swizzle row of 16-bit values
+constexpr int kBN = 128;          // weight rows (output features) per CTA
+constexpr int kTileM = 128;       // tokens per accumulator (MMA M)
+constexpr int kDeq = 128;         // dequant / epilogue threads (warps 2..5)
+constexpr int kThreads = 64 + kDeq;
+constexpr int kWin = 8;           // outliers per (row, chunk) held in registers
+constexpr int kSmemLimit = 227 * 1024;
+
+struct GemmParams {
+    CUtensorMap tm_x;    // X [M, K], box 64 x 128, 128-byte swizzle
+    CUtensorMap tm_q;    // indices [N, wpr] u32, box 8 x 128
+    CUtensorMap tm_lut;  // per-group codebooks [N, ngroups * 8] u32, box 8*NPG x 128
+    const uint16_t* lut; // per-row codebooks (ungrouped)
+    void* out;
+    const int32_t* off;
+    const uint16_t* ccols;
+    const void* cvals;   // e5m2 bytes (reference layout) or f32 deltas (prepacked)
+    const uint16_t* loraB;
+    const float* lorah;
+    const uint16_t* gamma;
+    float scale;
+    int r, M, N, K, ngroups, goff, log2G, chunk_m, ncsr;
+    int ksteps;          // ceil(K / 64)
+    int lsteps;          // ceil(r / 64) low-rank steps after the K steps
+    uint32_t mul16, mul31;
+    int vec_out;         // rows of out are 16-byte aligned
+};
+
+// Shared-memory plan of one CTA: kStages stages of [X tiles | W tile | index
+// tile | codebooks], each 1024-byte aligned (the swizzle atom), then the
+// mbarriers, the TMEM address and gamma.
+template <int NACC, int NPG>
+struct Plan {
+    static constexpr int kX = kTileM * kBK * 2;  // one accumulator's X tile
+    static constexpr int kWoff = NACC * kX;
+    static constexpr int kIdxOff = kWoff + kBN * kBK * 2;
+    static constexpr int kPlOff = kIdxOff + kBN * 32;
+    static constexpr int kStage = (kPlOff + kBN * 32 * NPG + 1023) / 1024 * 1024;
+    static constexpr int kTail = 1024;  // barriers, TMEM slot, gamma
+    static constexpr int kStages = (kSmemLimit - 1024 - kTail) / kStage > 6 ? 6 : (kSmemLimit - 1024 - kTail) / kStage;
+    static constexpr int kBarOff = kStages * kStage;
+    static constexpr int kGammaOff = kBarOff + 512;
+    static constexpr int kAlloc = kBarOff + kTail + 1024;  // + alignment slack
+    static constexpr uint32_t kTx = NACC * kX + kBN * 32 + kBN * 32 * NPG;
+    static_assert(kStages >= 2, "shared memory too small for a pipeline");
+};
+
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
+__device__ __forceinline__ uint16_t lds16(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void sts16(uint32_t a, uint16_t v) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(v) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (ActTraits<T>::kIsF16) {
+        return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+    } else {
+        return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
+               ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
+    }
+}
+
+// Byte address of element k (0..63) of a 128-byte row at `row_addr` (row
+// index `row`) in a K-major tile with the 128-byte swizzle: the 16-byte chunk
+// index is XORed with row % 8 (the layout TMA writes and tcgen05 reads).
+__device__ __forceinline__ uint32_t sw128_elem(uint32_t row_addr, int row, int k) {
+    return row_addr + ((((k >> 3) ^ row) & 7) << 4) + ((k & 7) << 1);
+}
+
+template <typename T, int NACC, int NPG, bool PREPACKED>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+    using P = Plan<NACC, NPG>;
+    constexpr bool GROUPED = NPG > 0;
+    constexpr int S = P::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sb = (raw + 1023u) & ~1023u;
+    uint8_t* sgen = smem_raw + (sb - raw);
+    const uint32_t bars = sb + P::kBarOff;
+    auto full_bar = [&](int s) { return bars + 8u * s; };            // TMA landed (or stage handed over)
+    auto wfull_bar = [&](int s) { return bars + 8u * (S + s); };     // operand tiles written by threads
+    auto empty_bar = [&](int s) { return bars + 8u * (2 * S + s); }; // MMAs reading the stage are done
+    const uint32_t acc_bar = bars + 8u * (3 * S);
+    const uint32_t tmem_slot = bars + 8u * (3 * S + 1);
+    float* gam = reinterpret_cast<float*>(sgen + P::kGammaOff);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kBN;
+    const int m0 = blockIdx.y * (NACC * kTileM);
+    const int steps = p.ksteps + p.lsteps;
+    const bool dora = p.r > 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(wfull_bar(s), kDeq);
+            mbar_init(empty_bar(s), 1);
+        }
+        mbar_init(acc_bar, 1);
+        mbar_fence_init();
+        tma_prefetch_desc(&p.tm_x);
+        tma_prefetch_desc(&p.tm_q);
+        if (GROUPED) tma_prefetch_desc(&p.tm_lut);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, NACC * kBN);
+        tmem_relinquish();
+    }
+    if (threadIdx.x >= 64) {
+        const int n = n0 + threadIdx.x - 64;
+        gam[threadIdx.x - 64] = (dora && n < p.N) ? f16_bits_to_f32(__ldg(p.gamma + n)) : 1.f;
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sgen + P::kBarOff + 8 * (3 * S + 1));
+
+    auto group_at = [&](int col) { return min((col + p.goff) >> p.log2G, p.ngroups - 1); };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int j = 0; j < steps; ++j) {
+                const int s = j % S, u = j / S;
+                if (u > 0 && !mbar_wait(empty_bar(s), (u - 1) & 1)) break;
+                issued = j + 1;
+                const uint32_t st = sb + s * P::kStage;
+                if (j < p.ksteps) {
+                    mbar_arrive_expect_tx(full_bar(s), P::kTx);
+#pragma unroll
+                    for (int a = 0; a < NACC; ++a)
+                        tma_load_2d(st + a * P::kX, &p.tm_x, full_bar(s), j * kBK, m0 + a * kTileM);
+                    tma_load_2d(st + P::kIdxOff, &p.tm_q, full_bar(s), j * (kBK / 8), n0);
+                    if constexpr (GROUPED) tma_load_2d(st + P::kPlOff, &p.tm_lut, full_bar(s), group_at(j * kBK) * 8, n0);
+                } else {
+                    mbar_arrive(full_bar(s));  // low-rank step: the dequant threads fill both operands
+                }
+            }
+            // no copy may still be landing when the CTA exits (matters only
+            // after a wait ran out): the last use of each stage has completed
+            for (int j = issued > S ? issued - S : 0; j < issued; ++j) mbar_wait(full_bar(j % S), (j / S) & 1);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issue
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16(ActTraits<T>::kIsF16 ? 0u : 1u, kTileM, kBN);
+            for (int j = 0; j < steps; ++j) {
+                const int s = j % S, u = j / S;
+                if (!mbar_wait(full_bar(s), u & 1) || !mbar_wait(wfull_bar(s), u & 1)) break;
+                tc_fence_after_sync();
+                const uint32_t st = sb + s * P::kStage;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint64_t bdesc = umma_desc_sw128(st + P::kWoff + kk * 32);
+#pragma unroll
+                    for (int a = 0; a < NACC; ++a)
+                        umma_f16(tmem + a * kBN, umma_desc_sw128(st + a * P::kX + kk * 32), bdesc, idesc,
+                                 (j | kk) != 0);
+                }
+                umma_commit(empty_bar(s));
+            }
+            umma_commit(acc_bar);  // completes once every issued MMA has
+        }
+    } else {
+        // ------------------------------------------------------- dequant rows
+        const int td = threadIdx.x - 64;
+        const int nl = td;  // local weight row of this thread
+        const int n = n0 + nl;
+        const bool nv = n < p.N;
+        const uint32_t m16 = p.mul16, m31 = p.mul31;
+        const int sw = (nl >> 2) & 1;  // which 16-byte half to read first (bank spread)
+        bool ok = true;
+
+        LutPlanes PR;  // per-row codebook (ungrouped)
+        if (!GROUPED) load_planes<T, PREPACKED>(p.lut, n, nv, PR);
+
+        // outliers of this row: entries of the current chunk in registers
+        // (first kWin), the next chunk's prefetched one chunk ahead
+        const bool outl = p.off != nullptr && nv;
+        const int32_t* orow = p.off + (int64_t)(nv ? n : 0) * (p.ncsr + 1);
+        int ob = 0, oe = 0, one = 0, row_end = 0;
+        uint32_t wc[kWin], wv[kWin], nc[kWin], nvv[kWin];
+        auto load_win = [&](int base, uint32_t (&c)[kWin], uint32_t (&v)[kWin]) {
+#pragma unroll
+            for (int e = 0; e < kWin; ++e) {
+                const int i = base + e;
+                const bool in = i < row_end;
+                c[e] = in ? (uint32_t)__ldg(p.ccols + i) : 0xFFFFu;
+                if (PREPACKED)
+                    v[e] = in ? __float_as_uint(__ldg(reinterpret_cast<const float*>(p.cvals) + i)) : 0u;
+                else
+                    v[e] = in ? (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i) : 0u;
+            }
+        };
+        if (outl) {
+            row_end = __ldg(orow + p.ncsr);
+            ob = __ldg(orow);
+            oe = __ldg(orow + 1);
+            one = p.ncsr > 1 ? __ldg(orow + 2) : oe;
+            load_win(ob, wc, wv);
+            load_win(oe, nc, nvv);
+        }
+        const int ksteps_per_chunk = p.chunk_m / kBK;
+
+        // patch one outlier at column kl (0..63) of this k step
+        auto patch = [&](uint32_t wrow, int kl, uint32_t v) {
+            const uint32_t a = sw128_elem(wrow, nl, kl);
+            if (PREPACKED) {
+                const float w = ActTraits<T>::bits_to_f32(lds16(a)) + __uint_as_float(v);
+                const T t = ActTraits<T>::from_f32(w);
+                sts16(a, *reinterpret_cast<const uint16_t*>(&t));
+            } else {
+                sts16(a, ActTraits<T>::from_f16_bits(fp8_byte_to_f16_bits((uint8_t)v)));
+            }
+        };
+
+        for (int j = 0; j < steps && ok; ++j) {
+            const int s = j % S, u = j / S;
+            if (!mbar_wait(full_bar(s), u & 1)) { ok = false; break; }
+            const uint32_t st = sb + s * P::kStage;
+            const uint32_t wrow = st + P::kWoff + nl * 128;
+            if (j < p.ksteps) {
+                const int k0 = j * kBK;
+                const uint32_t irow = st + P::kIdxOff + nl * 32;
+                const uint4 wA = lds128(irow + 16 * sw), wB = lds128(irow + 16 * (sw ^ 1));
+                const uint4 w03 = sw ? wB : wA, w47 = sw ? wA : wB;
+                LutPlanes P0, P1;
+                if constexpr (GROUPED) {
+                    const uint32_t prow = st + P::kPlOff + nl * (32 * NPG);
+                    planes_from_smem<T, PREPACKED>(prow, P0);
+                    if (NPG == 2) {
+                        const int slot = group_at(k0 + 32) - group_at(k0);
+                        planes_from_smem<T, PREPACKED>(prow + 32 * slot, P1);
+                    } else {
+                        P1 = P0;
+                    }
+                } else {
+                    P0 = PR;
+                    P1 = PR;
+                }
+                const uint32_t words[8] = {w03.x, w03.y, w03.z, w03.w, w47.x, w47.y, w47.z, w47.w};
+#pragma unroll
+                for (int wi = 0; wi < 8; ++wi) {
+                    const LutPlanes& PL = wi < 4 ? P0 : P1;
+                    const uint32_t w = words[wi];
+                    const uint32_t sa = w & 0x77777777u;
+                    const uint32_t ca = lop_and_or(mulhi(w, m31), 0x44444444u, 0x32103210u);
+                    uint32_t o0, o1, o2, o3;
+                    lookup4(PL, sa, ca, o0, o1);
+                    lookup4(PL, mulhi(sa, m16), mulhi(ca, m16), o2, o3);
+                    sts128(wrow + (((wi ^ nl) & 7) << 4), o0, o1, o2, o3);
+                }
+                if (outl) {
+                    const int c = k0 / p.chunk_m;
+                    if (j > 0 && j % ksteps_per_chunk == 0) {  // entering chunk c: rotate the windows
+                        ob = oe;
+                        oe = one;
+                        one = c + 2 <= p.ncsr ? __ldg(orow + c + 2) : oe;
+#pragma unroll
+                        for (int e = 0; e < kWin; ++e) {
+                            wc[e] = nc[e];
+                            wv[e] = nvv[e];
+                        }
+                        load_win(oe, nc, nvv);
+                    }
+                    // columns of this step relative to what the entries store
+                    const int cbase = PREPACKED ? k0 : k0 - c * p.chunk_m;
+#pragma unroll
+                    for (int e = 0; e < kWin; ++e) {
+                        const int kl = (int)wc[e] - cbase;
+                        if (ob + e < oe && kl >= 0 && kl < kBK) patch(wrow, kl, wv[e]);
+                    }
+                    for (int i = ob + kWin; i < oe; ++i) {  // rows with more than kWin outliers in this chunk
+                        const int kl = (int)__ldg(p.ccols + i) - cbase;
+                        if (kl >= 0 && kl < kBK)
+                            patch(wrow, kl,
+                                  PREPACKED ? __float_as_uint(__ldg(reinterpret_cast<const float*>(p.cvals) + i))
+                                            : (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i));
+                    }
+                }
+            } else {
+                // low-rank step: X <- s * H (tokens x r), W <- B (rows x r), zero past r
+                const int j0 = (j - p.ksteps) * kBK;
+#pragma unroll 1
+                for (int a = 0; a < NACC; ++a) {
+                    const int m = m0 + a * kTileM + td;
+                    const uint32_t xrow = st + a * P::kX + td * 128;
+#pragma unroll 1
+                    for (int ch = 0; ch < 8; ++ch) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const int jj = j0 + 8 * ch + e;
+                            f[e] = (m < p.M && jj < p.r) ? p.scale * __ldg(p.lorah + (int64_t)m * p.r + jj) : 0.f;
+                        }
+                        sts128(xrow + (((ch ^ td) & 7) << 4), pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
+                               pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
+                    }
+                }
+#pragma unroll 1
+                for (int ch = 0; ch < 8; ++ch) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int jj = j0 + 8 * ch + e;
+                        f[e] = (nv && jj < p.r) ? f16_bits_to_f32(__ldg(p.loraB + (int64_t)n * p.r + jj)) : 0.f;
+                    }
+                    sts128(wrow + (((ch ^ nl) & 7) << 4), pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
+                           pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
+                }
+            }
+            fence_proxy_async_smem();  // generic-proxy tile writes -> tensor core
+            mbar_arrive(wfull_bar(s));
+        }
+
+        // ------------------------------------------------------------ epilogue
+        if (!mbar_wait(acc_bar, 0)) ok = false;
+        tc_fence_after_sync();
+        const int qd = warp & 3;  // TMEM lanes 32*qd .. 32*qd+31 belong to this warp
+        T* out = reinterpret_cast<T*>(p.out);
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+            const int m = m0 + a * kTileM + 32 * qd + lane;
+#pragma unroll 1
+            for (int cc = 0; cc < kBN / 32; ++cc) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * qd) << 16) + a * kBN + 32 * cc, v);
+                tmem_ld_wait();
+                if (!ok || m >= p.M) continue;
+                const int nb = n0 + 32 * cc;
+                T* orow_out = out + (int64_t)m * p.N + nb;
+                if (p.vec_out && nb + 32 <= p.N) {
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int i = 8 * q4 + 2 * e;
+                            w[e] = pack2<T>(__uint_as_float(v[i]) * gam[32 * cc + i],
+                                            __uint_as_float(v[i + 1]) * gam[32 * cc + i + 1]);
+                        }
+                        *reinterpret_cast<uint4*>(orow_out + 8 * q4) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (nb + i < p.N) orow_out[i] = ActTraits<T>::from_f32(__uint_as_float(v[i]) * gam[32 * cc + i]);
+                }
+            }
+        }
+    }
+
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem, NACC * kBN);
+    }
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz, const char* what) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(WLQ_ERR_CUDA, "wlq_gemm: cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(WLQ_ERR_CUDA, "wlq_gemm: tensor map for %s rejected (CUresult %d)", what, (int)r);
+    return WLQ_OK;
+}
+
+template <typename T, int NACC, int NPG, bool PREPACKED>
+int launch_tiles(const GemmParams& p, cudaStream_t stream) {
+    using P = Plan<NACC, NPG>;
+    auto kern = gemm_kernel<T, NACC, NPG, PREPACKED>;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P::kAlloc);
+    if (e != cudaSuccess) return check_cuda(e, "gemm_kernel smem attribute");
+    const dim3 grid((unsigned)((p.N + kBN - 1) / kBN), (unsigned)((p.M + NACC * kTileM - 1) / (NACC * kTileM)));
+    kern<<<grid, kThreads, P::kAlloc, stream>>>(p);
+    return check_cuda(cudaGetLastError(), "gemm_kernel launch");
+}
+
+template <typename T, int NACC>
+int dispatch_npg(const GemmParams& p, int npg, bool prepacked, cudaStream_t stream) {
+    switch (npg) {
+        case 0: return prepacked ? launch_tiles<T, NACC, 0, true>(p, stream) : launch_tiles<T, NACC, 0, false>(p, stream);
+        case 1: return prepacked ? launch_tiles<T, NACC, 1, true>(p, stream) : launch_tiles<T, NACC, 1, false>(p, stream);
+        default: return prepacked ? launch_tiles<T, NACC, 2, true>(p, stream) : launch_tiles<T, NACC, 2, false>(p, stream);
+    }
+}
+
+// M > 16 shapes the TMA path cannot take run as decode GEMVs over 16-token slices.
+int gemm_by_slices(const LinearArgs& a, cudaStream_t stream) {
+    const size_t es = 2;
+    for (int m = 0; m < a.M; m += 16) {
+        LinearArgs s = a;
+        s.M = a.M - m < 16 ? a.M - m : 16;
+        s.x = static_cast<const char*>(a.x) + (size_t)m * a.K * es;
+        s.out = static_cast<char*>(a.out) + (size_t)m * a.N * es;
+        if (a.lorah) s.lorah = a.lorah + (size_t)m * a.r;
+        const int rc = launch_gemv(s, stream);
+        if (rc) return rc;
+    }
+    return WLQ_OK;
+}
+
+}  // namespace
+
+int launch_gemm(const LinearArgs& a, cudaStream_t stream) {
+    if (a.M == 0 || a.N == 0) return WLQ_OK;
+    int log2G = 0;
+    if (a.group_size > 0) {
+        while ((1 << log2G) < a.group_size) ++log2G;
+        if ((1 << log2G) != a.group_size || a.group_size < 32 || a.group_offset % 32 != 0)
+            return fail(WLQ_ERR_UNSUPPORTED,
+                        "wlq_gemm: per-group codebooks need a power-of-two group_size >= 32 and a group_offset "
+                        "multiple of 32 (got %d, %d)", a.group_size, a.group_offset);
+    }
+    const bool tma_ok = a.K % 8 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                        (a.off == nullptr || a.chunk_m % kBK == 0);
+    if (!tma_ok) return gemm_by_slices(a, stream);
+
+    GemmParams p;
+    memset(&p, 0, sizeof(p));
+    const CUtensorMapDataType xdt =
+        a.dtype == WLQ_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    int rc = encode_2d(&p.tm_x, xdt, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2, kBK, kTileM,
+                       CU_TENSOR_MAP_SWIZZLE_128B, "X");
+    if (rc) return rc;
+    rc = encode_2d(&p.tm_q, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.q, (uint64_t)a.wpr, (uint64_t)a.N, (uint64_t)a.wpr * 4,
+                   kBK / 8, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, "q_packed");
+    if (rc) return rc;
+    // codebooks per 64-column step: 1 when groups of >= 64 columns align with
+    // the steps, else 2 (a step then spans at most two groups)
+    const int npg = a.group_size == 0 ? 0 : (a.group_size >= kBK && a.group_offset % kBK == 0) ? 1 : 2;
+    if (npg > 0) {
+        rc = encode_2d(&p.tm_lut, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.lut, (uint64_t)a.ngroups * 8, (uint64_t)a.N,
+                       (uint64_t)a.ngroups * 32, 8 * npg, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, "lut_c");
+        if (rc) return rc;
+    }
+    p.lut = a.lut; p.out = a.out; p.off = a.off; p.ccols = a.ccols; p.cvals = a.cvals;
+    p.loraB = a.loraB; p.lorah = a.lorah; p.gamma = a.gamma; p.scale = a.scale;
+    p.r = a.r; p.M = a.M; p.N = a.N; p.K = a.K;
+    p.ngroups = a.ngroups; p.goff = a.group_offset; p.log2G = log2G;
+    p.chunk_m = a.chunk_m; p.ncsr = a.ncsr;
+    p.ksteps = (a.K + kBK - 1) / kBK;
+    p.lsteps = a.r > 0 ? (a.r + kBK - 1) / kBK : 0;
+    p.mul16 = 1u << 16;
+    p.mul31 = 1u << 31;
+    p.vec_out = (a.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0);
+
+    // two accumulators (256 tokens per CTA) halve the dequantisation per FLOP
+    // once there are enough tiles to fill the GPU
+    const int sms = device_sm_count();
+    const int64_t ntiles = (a.N + kBN - 1) / kBN;
+    const bool two = ((int64_t)(a.M + 2 * kTileM - 1) / (2 * kTileM)) * ntiles >= sms;
+    if (a.dtype == WLQ_DTYPE_BF16)
+        return two ? dispatch_npg<__nv_bfloat16, 2>(p, npg, a.lut_prepacked, stream)
+                   : dispatch_npg<__nv_bfloat16, 1>(p, npg, a.lut_prepacked, stream);
+    return two ? dispatch_npg<__half, 2>(p, npg, a.lut_prepacked, stream)
+               : dispatch_npg<__half, 1>(p, npg, a.lut_prepacked, stream);
+}
+
+int read_device_error(int device, unsigned int* flags, int clear) {
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return check_cuda(e, "cudaGetDevice");
+    if (device != prev && (e = cudaSetDevice(device)) != cudaSuccess) return check_cuda(e, "cudaSetDevice");
+    unsigned int v = 0;
+    e = cudaMemcpyFromSymbol(&v, g_wlq_device_error, sizeof(v));
+    if (e == cudaSuccess && clear) {
+        const unsigned int z = 0;
+        e = cudaMemcpyToSymbol(g_wlq_device_error, &z, sizeof(z));
+    }
+    if (device != prev) cudaSetDevice(prev);
+    if (e != cudaSuccess) return check_cuda(e, "device error word");
+    *flags = v;
+    return WLQ_OK;
+}
+
 }  // namespace wlq

@@ -49,6 +49,9 @@ int launch_dequant(const uint32_t* q, const uint16_t* lut, uint16_t* W, const in
                    int group_size, int group_offset, int ngroups, int chunk_m, int ncsr,
                    cudaStream_t stream);
 
+// Reads (and optionally clears) the device error word of `device`.
+int read_device_error(int device, unsigned int* flags, int clear);
+
 // Multiprocessor count of the current device (cached per device).
 int device_sm_count();
 

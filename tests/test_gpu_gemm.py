@@ -1,0 +1,115 @@
+"""Parity of the tensor-core prefill GEMM (wlq_gemm, M > 16) with the oracle:
+per-row and per-group codebooks (steps spanning one or two groups), both
+codebook/outlier layouts, ragged M / N / K, rows dense with outliers, the
+low-rank term folded in as extra K steps, and the shapes that fall back to
+16-token GEMV slices.  B200 only."""
+import numpy as np
+import pytest
+import torch
+
+from _gpu import C, dev_layer, inputs, run_ours
+from _layers import make_np_layer, reference_output, rel_err
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float16: 5e-3, torch.bfloat16: 2e-2}  # normwise max relative error
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    assert torch.cuda.is_available(), "the gpu tests need a CUDA device"
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    assert C().device_error() == 0  # no bounded wait ran out in this module
+
+
+GEMM_CASES = [
+    # N, K, G, goff, outliers, dora
+    (128, 1024, 0, 0, True, True),     # per-row codebooks, one N tile
+    (300, 1536, 128, 0, True, True),   # N not a multiple of 8 (scalar stores), 128-wide groups
+    (256, 1088, 128, 64, True, True),  # shard starting mid-group: steps span two groups
+    (130, 1024, 32, 0, True, False),   # 32-wide groups: two groups per step
+    (200, 2048, 64, 32, True, True),   # 64-wide groups offset by 32
+    (96, 1096, 0, 0, True, True),      # K not a multiple of 64: ragged last step
+    (64, 512, 128, 0, False, False),   # no outliers, no low-rank term
+    (40, 203, 0, 0, True, True),       # K % 8 != 0: 16-token GEMV slices
+]
+
+
+@pytest.mark.parametrize("case", GEMM_CASES, ids=lambda c: f"N{c[0]}K{c[1]}G{c[2]}o{c[3]}")
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_gemm_matches_oracle(case, dtype):
+    N, K, G, goff, outl, dora = case
+    rng = np.random.default_rng(7 * N + K + G)
+    L = make_np_layer(rng, N, K, G, goff, density=0.02, outliers=outl, dora=dora)
+    T = dev_layer(L)
+    for M in (17, 128, 200, 300):
+        x, h = inputs(rng, L, M, dtype)
+        ref = reference_output(L, x.float().cpu().numpy(), None if h is None else h.cpu().numpy())
+        ys = []
+        for fmt in (0, 1):
+            y = run_ours(L, T, x, h, fmt=fmt)
+            assert torch.isfinite(y).all(), (M, fmt)
+            e = rel_err(y.float().cpu().numpy(), ref)
+            assert e <= TOL[dtype], (M, fmt, e)
+            ys.append(y.float())
+        # the two layouts patch the same outlier values into the tile
+        assert rel_err(ys[1].cpu().numpy(), ys[0].cpu().numpy()) <= 1e-3, M
+
+
+def test_gemm_outlier_edges():
+    """Outliers at the first and last column, a row made only of outliers
+    (more per chunk than the per-thread window), a run across a step
+    boundary, and rows without any; two N tiles, M spanning two accumulators."""
+    rng = np.random.default_rng(78)
+    N, K = 160, 1096
+    L = make_np_layer(rng, N, K, 128, 0, outliers=False, dora=True)
+    mask = np.zeros((N, K), bool)
+    mask[0, 0] = mask[0, K - 1] = True
+    mask[1, 1024:] = True
+    mask[2, :] = True
+    mask[5, 60:70] = True
+    mask[129, 500:530] = True
+    mask[150:160, ::97] = True
+    L.off, L.cols = O.build_chunk_csr(mask, 512)
+    L.vals = O.fp16_to_fp8_bytes((rng.standard_normal(L.cols.size) * 0.1).astype(np.float16))
+    T = dev_layer(L)
+    for M in (33, 257):
+        for dtype in (torch.float16, torch.bfloat16):
+            x, h = inputs(rng, L, M, dtype)
+            ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+            for fmt in (0, 1):
+                y = run_ours(L, T, x, h, fmt=fmt)
+                assert rel_err(y.float().cpu().numpy(), ref) <= TOL[dtype], (M, dtype, fmt)
+
+
+def test_gemm_rank_above_one_step():
+    """A low-rank term of rank 80 takes two extra K steps."""
+    rng = np.random.default_rng(5)
+    L = make_np_layer(rng, 128, 512, 128, 0, density=0.01, r=80)
+    T = dev_layer(L)
+    x, h = inputs(rng, L, 150, torch.float16)
+    ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+    y = run_ours(L, T, x, h)
+    assert rel_err(y.float().cpu().numpy(), ref) <= TOL[torch.float16]
+
+
+@pytest.mark.parametrize("name,M", [("qkv", 512), ("o", 2048), ("down", 512)])
+def test_gemm_full_size_shapes(name, M):
+    """BASELINE config-2 shapes with the benchmark recipe against the
+    dequantised weights times x in fp32 on the GPU."""
+    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+    K, N = S.QWEN25_7B[name]
+    L = S.make_layer(N, K, group_size=128, density=0.005, r=16, seed=12)
+    W = torch.empty((N, K), dtype=torch.float16, device="cuda")
+    C().dequant_w0(L.q_packed, L.lut_c, W, N, K, 4, L.words_per_row, L.chunk_offsets, L.chunk_cols, L.chunk_vals,
+                   128, 0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4)
+    x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+    h = S.lora_h(L, x)
+    y = S.forward(L, x, h=h)
+    ref = (x.float() @ W.float().t() + L.lora_scale * (h @ L.lora_B.float().t())) * L.dora_gamma.float()
+    e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert e <= 2e-2, (name, M, e)
