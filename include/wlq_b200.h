@@ -66,9 +66,10 @@ enum wlq_dtype { WLQ_DTYPE_F16 = 0, WLQ_DTYPE_BF16 = 1 };
  * WLQ_LUT_PREPACKED: the load-time layout for one act_dtype, made once by
  * wlq_prepack_lut (codebooks: entries rounded to the MMA type, bytes split
  * into planes; same size and indexing) and wlq_prepack_outliers (chunk_cols
- * then holds uint16 global columns and chunk_vals points to float32
- * corrections w_outlier - codebook value; chunk_offsets unchanged), so the
- * kernels never convert codebooks or look up outlier codebook values. */
+ * then points to uint32 records, column | outlier value bits in the MMA type
+ * << 16, each row's entries in ascending column order, and chunk_vals to
+ * float32 corrections w_outlier - codebook value; chunk_offsets unchanged),
+ * so the kernels never convert codebooks or look up outlier codebook values. */
 enum wlq_lut_format { WLQ_LUT_F16 = 0, WLQ_LUT_PREPACKED = 1 };
 
 /* Message of the last failed call on this thread ("" if none). */
@@ -84,18 +85,20 @@ WLQ_API int wlq_abi_version(void);
  * gemv_forward (csrc/vllm_binding.cpp:253-315), which handle M = 1 only and
  * need a split-K workspace; this one needs none.  bits must be 4. */
 WLQ_API int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, void* out,
-             const int32_t* chunk_offsets, const uint16_t* chunk_cols, const uint8_t* chunk_vals,
+             const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
              const void* lora_B, const float* lora_h, const void* dora_gamma, float lora_scale,
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
              int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
 
 /* Batched forward for any M >= 1: M <= 16 runs the GEMV-class kernel, larger
  * M the tcgen05 tensor-core GEMM with dequantisation, outlier replacement and
- * the DoRA epilogue fused.  Replaces launch_gemm_metalog_dora
+ * the DoRA epilogue fused.  chunk_cols / chunk_vals: uint16 columns and e5m2
+ * bytes (WLQ_LUT_F16) or the prepacked records and corrections
+ * (WLQ_LUT_PREPACKED).  Replaces launch_gemm_metalog_dora
  * (csrc/gemm_kernel.cu:527-547) and the M >= 16 dequantise + cuBLAS +
  * epilogue composition of gemm_forward (csrc/vllm_binding.cpp:318-419). */
 WLQ_API int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* out,
-             const int32_t* chunk_offsets, const uint16_t* chunk_cols, const uint8_t* chunk_vals,
+             const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
              const float* lora_H, const void* lora_B, const void* dora_gamma, float lora_scale,
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
              int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
@@ -108,15 +111,19 @@ WLQ_API int wlq_prepack_lut(const void* lut_c, void* lut_out, int64_t n_codebook
                             wlq_stream_t stream);
 
 /* Outliers -> the WLQ_LUT_PREPACKED outlier stream for act_dtype: per chunk-CSR
- * entry, in the same order, the global column (uint16, K <= 65535; 0xFFFF for
- * an entry past K) and the float32 correction w_outlier - codebook value with
- * the codebook entry rounded to the MMA type.  Inputs are in the reference
- * layout (fp16 codebooks).  No reference counterpart (the reference re-reads
- * the index word and codebook per outlier, csrc/gemv_kernel.cu:262-288). */
+ * entry a uint32 record (global column in the low 16 bits, K <= 65535, 0xFFFF
+ * for an entry past K; the outlier value rounded to the MMA type in the high
+ * 16 bits) and the float32 correction w_outlier - codebook value with the
+ * codebook entry rounded to the MMA type.  Within each row the entries are
+ * reordered by ascending column (they stay inside their chunk's index range;
+ * the reference's builders already emit that order).  Inputs are in the
+ * reference layout (fp16 codebooks).  No reference counterpart (the reference
+ * re-reads the index word and codebook per outlier,
+ * csrc/gemv_kernel.cu:262-288). */
 WLQ_API int wlq_prepack_outliers(const int32_t* q_packed, const void* lut_c, const int32_t* chunk_offsets,
                                  const uint16_t* chunk_cols, const uint8_t* chunk_vals, int64_t nnz, int N,
                                  int K, int bits, int words_per_row, int lut_group_size, int lut_group_offset,
-                                 int act_dtype, uint16_t* cols_out, float* delta_out, wlq_stream_t stream);
+                                 int act_dtype, uint32_t* cols_out, float* delta_out, wlq_stream_t stream);
 
 /* Dense fp16 W[N, K] (codebook gather, then outliers overwritten), bit-exact
  * with the reference.  bits 1..4.  Replaces launch_dequant_patch_metalog

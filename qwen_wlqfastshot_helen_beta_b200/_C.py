@@ -89,7 +89,8 @@ def _linear_checks(name, x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, v
         chunk_m = 640 if bits == 3 else 512
         nc = (K + chunk_m - 1) // chunk_m
         _check_opt(name, "chunk_offsets", offs, torch.int32, dev)
-        _check_opt(name, "chunk_cols", cols, torch.uint16, dev)
+        # prepacked layers carry uint32 records (column | value << 16)
+        _check_opt(name, "chunk_cols", cols, torch.int32 if lut_format == WLQ_LUT_PREPACKED else torch.uint16, dev)
         # prepacked layers carry float32 corrections in place of e5m2 bytes
         _check_opt(name, "chunk_vals", vals, torch.float32 if lut_format == WLQ_LUT_PREPACKED else torch.uint8, dev)
         _require(offs.numel() == N * (nc + 1), f"{name}: chunk_offsets must be [{N}, {nc + 1}]")
@@ -215,8 +216,10 @@ def prepack_lut(lut_c: torch.Tensor, act_dtype: torch.dtype) -> torch.Tensor:
 
 def prepack_outliers(q_packed, lut_c, chunk_offsets, chunk_cols, chunk_vals, N, K, bits, act_dtype,
                      lut_group_size=0, lut_group_offset=0):
-    """Reference-layout outliers -> (uint16 global columns, float32 corrections)
-    for `act_dtype`, the WLQ_LUT_PREPACKED outlier stream (CUDA tensors)."""
+    """Reference-layout outliers -> (int32 records: global column | value in
+    the MMA type << 16, float32 corrections) for `act_dtype`, the
+    WLQ_LUT_PREPACKED outlier stream (CUDA tensors; each row's entries in
+    ascending column order)."""
     offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
     if offs is None or cols is None or vals is None:
         return None, None
@@ -225,7 +228,7 @@ def prepack_outliers(q_packed, lut_c, chunk_offsets, chunk_cols, chunk_vals, N, 
                   ("chunk_vals", vals)):
         _require(t.is_cuda and t.device == dev and t.is_contiguous(), f"prepack_outliers: {nm} must be on {dev}")
     _require(vals.dtype == torch.uint8 and cols.dtype == torch.uint16, "prepack_outliers: e5m2 bytes / uint16 cols")
-    gcols = torch.empty_like(cols)
+    gcols = torch.empty(cols.numel(), dtype=torch.int32, device=dev)
     delta = torch.empty(cols.numel(), dtype=torch.float32, device=dev)
     dt = WLQ_DTYPE_BF16 if act_dtype == torch.bfloat16 else WLQ_DTYPE_F16
     with _DeviceGuard(dev):

@@ -59,7 +59,7 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 
 // Shared validation of the quantized-linear arguments.
 int build_args(const char* fn, const void* x, const int32_t* q, const void* lut, void* out,
-               const int32_t* off, const uint16_t* ccols, const uint8_t* cvals, const void* loraB,
+               const int32_t* off, const void* ccols, const void* cvals, const void* loraB,
                const float* lorah, const void* gamma, float scale, int r, int M, int N, int K, int bits,
                int wpr, int G, int goff, int lut_format, int dtype, LinearArgs& a) {
     if (M < 0 || N < 0 || K < 0) return fail(WLQ_ERR_INVALID_ARG, "%s: negative size (M=%d N=%d K=%d)", fn, M, N, K);
@@ -82,6 +82,8 @@ int build_args(const char* fn, const void* x, const int32_t* q, const void* lut,
         return fail(WLQ_ERR_ALIGNMENT, "%s: q_packed and lut_c must be 16-byte aligned", fn);
     if (!aligned(x, 2) || !aligned(out, 2)) return fail(WLQ_ERR_ALIGNMENT, "%s: x/out must be 2-byte aligned", fn);
     const bool has_outl = off && ccols && cvals;
+    if (has_outl && lut_format == WLQ_LUT_PREPACKED && K > 65535)
+        return fail(WLQ_ERR_UNSUPPORTED, "%s: prepacked outliers hold uint16 columns; K=%d is too large", fn, K);
     const bool dora = loraB && lorah && gamma && r > 0;
     a.q = reinterpret_cast<const uint32_t*>(q);
     a.lut = reinterpret_cast<const uint16_t*>(lut);
@@ -127,7 +129,7 @@ const char* wlq_last_error(void) { return g_last_error; }
 int wlq_abi_version(void) { return WLQ_ABI_VERSION; }
 
 int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, void* out, const int32_t* chunk_offsets,
-             const uint16_t* chunk_cols, const uint8_t* chunk_vals, const void* lora_B, const float* lora_h,
+             const void* chunk_cols, const void* chunk_vals, const void* lora_B, const float* lora_h,
              const void* dora_gamma, float lora_scale, int r, int M, int N, int K, int bits, int words_per_row,
              int lut_group_size, int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream) {
     g_last_error[0] = '\0';
@@ -143,7 +145,7 @@ int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, void* ou
 }
 
 int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* out, const int32_t* chunk_offsets,
-             const uint16_t* chunk_cols, const uint8_t* chunk_vals, const float* lora_H, const void* lora_B,
+             const void* chunk_cols, const void* chunk_vals, const float* lora_H, const void* lora_B,
              const void* dora_gamma, float lora_scale, int r, int M, int N, int K, int bits, int words_per_row,
              int lut_group_size, int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream) {
     g_last_error[0] = '\0';
@@ -207,7 +209,7 @@ int wlq_prepack_lut(const void* lut_c, void* lut_out, int64_t n_codebooks, int a
 int wlq_prepack_outliers(const int32_t* q_packed, const void* lut_c, const int32_t* chunk_offsets,
                          const uint16_t* chunk_cols, const uint8_t* chunk_vals, int64_t nnz, int N, int K, int bits,
                          int words_per_row, int lut_group_size, int lut_group_offset, int act_dtype,
-                         uint16_t* cols_out, float* delta_out, wlq_stream_t stream) {
+                         uint32_t* cols_out, float* delta_out, wlq_stream_t stream) {
     g_last_error[0] = '\0';
     if (nnz < 0 || N < 0 || K < 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_prepack_outliers: negative size");
     if (bits != 4) return fail(WLQ_ERR_UNSUPPORTED, "wlq_prepack_outliers: 4-bit indices only (bits=%d)", bits);

@@ -156,30 +156,49 @@ __global__ void prepack_outliers_kernel(const uint32_t* __restrict__ q, const ui
                                         const int32_t* __restrict__ off, const uint16_t* __restrict__ ccols,
                                         const uint8_t* __restrict__ cvals, int N, int K, int wpr, int log2G,
                                         bool grouped, int goff, int ngroups, int chunk_m, int ncsr,
-                                        uint16_t* __restrict__ gcols, float* __restrict__ delta) {
+                                        uint32_t* __restrict__ recs, float* __restrict__ delta) {
     for (int row = blockIdx.x * blockDim.x + threadIdx.x; row < N; row += gridDim.x * blockDim.x) {
         const int32_t* ro = off + (int64_t)row * (ncsr + 1);
         for (int cc = 0; cc < ncsr; ++cc) {
             for (int i = ro[cc]; i < ro[cc + 1]; ++i) {
                 const int col = cc * chunk_m + ccols[i];
                 float d = 0.f;
+                uint32_t vbits = 0u;
                 if (col < K) {
                     const uint32_t sym = (q[(int64_t)row * wpr + (col >> 3)] >> (4 * (col & 7))) & 15u;
                     const int grp = grouped ? (col + goff) >> log2G : 0;
                     const uint16_t lb = lut[((int64_t)row * ngroups + grp) * 16 + sym];
                     const float wl = ActTraits<T>::bits_to_f32(ActTraits<T>::from_f16_bits(lb));
-                    d = f16_bits_to_f32(fp8_byte_to_f16_bits(cvals[i])) - wl;
+                    const uint16_t ob = fp8_byte_to_f16_bits(cvals[i]);
+                    d = f16_bits_to_f32(ob) - wl;
+                    vbits = ActTraits<T>::from_f16_bits(ob);  // exact: e5m2 fits both types
                 }
-                gcols[i] = (uint16_t)(col < K ? col : 0xFFFF);  // 0xFFFF: dropped (past K)
+                recs[i] = (col < K ? (uint32_t)col : 0xFFFFu) | (vbits << 16);  // 0xFFFF: dropped (past K)
                 delta[i] = d;
             }
+        }
+        // order the row by column (the builders of the reference layout emit
+        // sorted chunks, so this is one pass; entries stay inside their chunk's
+        // index range because chunks partition the columns)
+        for (int i = ro[0] + 1; i < ro[ncsr]; ++i) {
+            const uint32_t c = recs[i];
+            if ((recs[i - 1] & 0xFFFFu) <= (c & 0xFFFFu)) continue;
+            const float d = delta[i];
+            int k = i - 1;
+            while (k >= ro[0] && (recs[k] & 0xFFFFu) > (c & 0xFFFFu)) {
+                recs[k + 1] = recs[k];
+                delta[k + 1] = delta[k];
+                --k;
+            }
+            recs[k + 1] = c;
+            delta[k + 1] = d;
         }
     }
 }
 
 int launch_prepack_outliers(const uint32_t* q, const uint16_t* lut, const int32_t* off, const uint16_t* ccols,
                             const uint8_t* cvals, int N, int K, int wpr, int group_size, int goff, int ngroups,
-                            int chunk_m, int ncsr, int dtype, uint16_t* gcols, float* delta, cudaStream_t stream) {
+                            int chunk_m, int ncsr, int dtype, uint32_t* recs, float* delta, cudaStream_t stream) {
     int log2G = 0;
     if (group_size > 0) {
         while ((1 << log2G) < group_size) ++log2G;
@@ -190,10 +209,10 @@ int launch_prepack_outliers(const uint32_t* q, const uint16_t* lut, const int32_
     const int blocks = (N + threads - 1) / threads;
     if (dtype == WLQ_DTYPE_BF16)
         prepack_outliers_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(
-            q, lut, off, ccols, cvals, N, K, wpr, log2G, group_size > 0, goff, ngroups, chunk_m, ncsr, gcols, delta);
+            q, lut, off, ccols, cvals, N, K, wpr, log2G, group_size > 0, goff, ngroups, chunk_m, ncsr, recs, delta);
     else
         prepack_outliers_kernel<__half><<<blocks, threads, 0, stream>>>(
-            q, lut, off, ccols, cvals, N, K, wpr, log2G, group_size > 0, goff, ngroups, chunk_m, ncsr, gcols, delta);
+            q, lut, off, ccols, cvals, N, K, wpr, log2G, group_size > 0, goff, ngroups, chunk_m, ncsr, recs, delta);
     return check_cuda(cudaGetLastError(), "prepack_outliers_kernel launch");
 }
 

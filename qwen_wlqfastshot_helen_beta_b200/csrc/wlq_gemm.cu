@@ -9,7 +9,7 @@
 //   warp 0      TMA producer: X tiles (64 k x 128 tokens, 128-byte swizzle),
 //               the 128 x 64 index tile and its codebooks, per pipeline stage;
 //   warp 1      allocates TMEM and issues tcgen05.mma from one thread;
-//   warps 2..5  one weight row per thread: LUT lookups in registers (byte
+//   warps 2..9  two threads per weight row: LUT lookups in registers (byte
 //               permutes, as in the decode GEMV) written as the K-major
 //               128-byte-swizzled bf16/f16 tile the MMA reads, outlier values
 //               patched in, then the epilogue (TMEM -> gamma -> global).
@@ -34,9 +34,16 @@ namespace {
 constexpr int kBK = 64;           // k per stage: one 128-byte swizzle row of 16-bit values
 constexpr int kBN = 128;          // weight rows (output features) per CTA
 constexpr int kTileM = 128;       // tokens per accumulator (MMA M)
-constexpr int kDeq = 128;         // dequant / epilogue threads (warps 2..5)
+#ifndef WLQ_GEMM_TPR
+#define WLQ_GEMM_TPR 4
+#endif
+constexpr int kTpr = WLQ_GEMM_TPR;   // dequant threads per weight row
+constexpr int kDeq = 128 * kTpr;     // dequant / epilogue threads (warps 2 ..)
+constexpr int kColsT = kBK / kTpr;   // columns of a step per dequant thread (<= 32: one codebook group)
+constexpr int kWordsT = kColsT / 8;  // index words per dequant thread
 constexpr int kThreads = 64 + kDeq;
-constexpr int kWin = 8;           // outliers per (row, chunk) held in registers
+constexpr int kWin = 8;           // reference layout: outliers per (row, chunk) held in registers
+constexpr int kStream = 4;        // prepacked layout: sorted outliers per row held in registers
 constexpr int kSmemLimit = 227 * 1024;
 
 struct GemmParams {
@@ -46,8 +53,8 @@ struct GemmParams {
     const uint16_t* lut; // per-row codebooks (ungrouped)
     void* out;
     const int32_t* off;
-    const uint16_t* ccols;
-    const void* cvals;   // e5m2 bytes (reference layout) or f32 deltas (prepacked)
+    const void* ccols;   // uint16 chunk-local columns, or uint32 records column | value << 16 (prepacked)
+    const void* cvals;   // e5m2 bytes (reference layout); unused when prepacked
     const uint16_t* loraB;
     const float* lorah;
     const uint16_t* gamma;
@@ -81,9 +88,9 @@ struct Plan {
 __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
-__device__ __forceinline__ uint16_t lds16(uint32_t a) {
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a) : "memory");
     return v;
 }
 __device__ __forceinline__ void sts16(uint32_t a, uint16_t v) {
@@ -126,8 +133,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kBN;
-    const int m0 = blockIdx.y * (NACC * kTileM);
+    // token tiles vary fastest across the launch, so the CTAs resident at
+    // one time read several activation tiles instead of all hitting one
+    const int mtiles = (p.M + NACC * kTileM - 1) / (NACC * kTileM);
+    const int n0 = (int)(blockIdx.x / mtiles) * kBN;
+    const int m0 = (int)(blockIdx.x % mtiles) * (NACC * kTileM);
     const int steps = p.ksteps + p.lsteps;
     const bool dora = p.r > 0;
 
@@ -147,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         tmem_alloc(tmem_slot, NACC * kBN);
         tmem_relinquish();
     }
-    if (threadIdx.x >= 64) {
+    if (threadIdx.x >= 64 && threadIdx.x < 64 + kBN) {
         const int n = n0 + threadIdx.x - 64;
         gam[threadIdx.x - 64] = (dora && n < p.N) ? f16_bits_to_f32(__ldg(p.gamma + n)) : 1.f;
     }
@@ -205,55 +215,78 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
     } else {
         // ------------------------------------------------------- dequant rows
+        // kTpr threads per weight row: thread (nl, part) owns columns
+        // [kColsT part, kColsT part + kColsT) of every step (kWordsT index
+        // words, one codebook: groups are >= 32 columns and 32-aligned)
         const int td = threadIdx.x - 64;
-        const int nl = td;  // local weight row of this thread
+        const int nl = td / kTpr;
+        const int part = td % kTpr;
+        const int col0 = kColsT * part;
         const int n = n0 + nl;
         const bool nv = n < p.N;
         const uint32_t m16 = p.mul16, m31 = p.mul31;
-        const int sw = (nl >> 2) & 1;  // which 16-byte half to read first (bank spread)
         bool ok = true;
 
         LutPlanes PR;  // per-row codebook (ungrouped)
         if (!GROUPED) load_planes<T, PREPACKED>(p.lut, n, nv, PR);
 
-        // outliers of this row: entries of the current chunk in registers
-        // (first kWin), the next chunk's prefetched one chunk ahead
+        // outliers of this row.  Prepacked layout: the row's entries are
+        // sorted by global column and stream through two kStream-entry
+        // register windows: entries are consumed from the current one by
+        // index, and the other, loaded a whole window earlier, replaces it
+        // when it runs out (no read waits on a load just issued).  Reference
+        // layout: the first kWin entries of the current chunk in registers,
+        // the next chunk's prefetched one chunk ahead.
         const bool outl = p.off != nullptr && nv;
         const int32_t* orow = p.off + (int64_t)(nv ? n : 0) * (p.ncsr + 1);
-        int ob = 0, oe = 0, one = 0, row_end = 0;
+        int ob = 0, oe = 0, one = 0, row_end = 0, li = 0;
         uint32_t wc[kWin], wv[kWin], nc[kWin], nvv[kWin];
+        int head = 0;  // prepacked: next entry of window wc/wv
         auto load_win = [&](int base, uint32_t (&c)[kWin], uint32_t (&v)[kWin]) {
 #pragma unroll
             for (int e = 0; e < kWin; ++e) {
                 const int i = base + e;
                 const bool in = i < row_end;
-                c[e] = in ? (uint32_t)__ldg(p.ccols + i) : 0xFFFFu;
-                if (PREPACKED)
-                    v[e] = in ? __float_as_uint(__ldg(reinterpret_cast<const float*>(p.cvals) + i)) : 0u;
-                else
-                    v[e] = in ? (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i) : 0u;
+                c[e] = in ? (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(p.ccols) + i) : 0xFFFFu;
+                v[e] = in ? (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i) : 0u;
             }
+        };
+        // next record of the sorted stream (column | value << 16); nothing
+        // here waits on the load (a record is first used a window later).
+        // Column 0xFFFF (an entry past K, sorted last, or the end of the row)
+        // is never below a step's end because K <= 65535.
+        auto pull = [&](uint32_t& rec) {
+            const bool in = li < row_end;
+            rec = in ? __ldg(reinterpret_cast<const uint32_t*>(p.ccols) + li) : 0xFFFFu;
+            li += in ? 1 : 0;
         };
         if (outl) {
             row_end = __ldg(orow + p.ncsr);
             ob = __ldg(orow);
-            oe = __ldg(orow + 1);
-            one = p.ncsr > 1 ? __ldg(orow + 2) : oe;
-            load_win(ob, wc, wv);
-            load_win(oe, nc, nvv);
+            if constexpr (PREPACKED) {
+                li = ob;
+#pragma unroll
+                for (int e = 0; e < kStream; ++e) pull(wc[e]);
+#pragma unroll
+                for (int e = 0; e < kStream; ++e) pull(nc[e]);
+            } else {
+                oe = __ldg(orow + 1);
+                one = p.ncsr > 1 ? __ldg(orow + 2) : oe;
+                load_win(ob, wc, wv);
+                load_win(oe, nc, nvv);
+            }
         }
         const int ksteps_per_chunk = p.chunk_m / kBK;
+        int chunk = 0, chunk_left = ksteps_per_chunk;  // reference layout: chunk of the current step
 
-        // patch one outlier at column kl (0..63) of this k step
+        // replaces the weight at column kl (0..63) of this step: v is the
+        // value in the MMA type (prepacked) or the e5m2 byte
         auto patch = [&](uint32_t wrow, int kl, uint32_t v) {
             const uint32_t a = sw128_elem(wrow, nl, kl);
-            if (PREPACKED) {
-                const float w = ActTraits<T>::bits_to_f32(lds16(a)) + __uint_as_float(v);
-                const T t = ActTraits<T>::from_f32(w);
-                sts16(a, *reinterpret_cast<const uint16_t*>(&t));
-            } else {
+            if (PREPACKED)
+                sts16(a, (uint16_t)v);
+            else
                 sts16(a, ActTraits<T>::from_f16_bits(fp8_byte_to_f16_bits((uint8_t)v)));
-            }
         };
 
         for (int j = 0; j < steps && ok; ++j) {
@@ -263,84 +296,112 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             const uint32_t wrow = st + P::kWoff + nl * 128;
             if (j < p.ksteps) {
                 const int k0 = j * kBK;
-                const uint32_t irow = st + P::kIdxOff + nl * 32;
-                const uint4 wA = lds128(irow + 16 * sw), wB = lds128(irow + 16 * (sw ^ 1));
-                const uint4 w03 = sw ? wB : wA, w47 = sw ? wA : wB;
-                LutPlanes P0, P1;
-                if constexpr (GROUPED) {
-                    const uint32_t prow = st + P::kPlOff + nl * (32 * NPG);
-                    planes_from_smem<T, PREPACKED>(prow, P0);
-                    if (NPG == 2) {
-                        const int slot = group_at(k0 + 32) - group_at(k0);
-                        planes_from_smem<T, PREPACKED>(prow + 32 * slot, P1);
-                    } else {
-                        P1 = P0;
-                    }
+                uint32_t words[kWordsT];
+                if constexpr (kWordsT == 4) {
+                    const uint4 w4 = lds128(st + P::kIdxOff + nl * 32 + col0 / 2);
+                    words[0] = w4.x; words[1] = w4.y; words[2] = w4.z; words[3] = w4.w;
                 } else {
-                    P0 = PR;
-                    P1 = PR;
+                    const uint2 w2 = lds64(st + P::kIdxOff + nl * 32 + col0 / 2);
+                    words[0] = w2.x; words[1] = w2.y;
                 }
-                const uint32_t words[8] = {w03.x, w03.y, w03.z, w03.w, w47.x, w47.y, w47.z, w47.w};
+                LutPlanes PL;
+                if constexpr (GROUPED) {
+                    const int slot = NPG == 2 ? group_at(k0 + col0) - group_at(k0) : 0;
+                    planes_from_smem<T, PREPACKED>(st + P::kPlOff + nl * (32 * NPG) + 32 * slot, PL);
+                } else {
+                    PL = PR;
+                }
 #pragma unroll
-                for (int wi = 0; wi < 8; ++wi) {
-                    const LutPlanes& PL = wi < 4 ? P0 : P1;
+                for (int wi = 0; wi < kWordsT; ++wi) {
                     const uint32_t w = words[wi];
                     const uint32_t sa = w & 0x77777777u;
                     const uint32_t ca = lop_and_or(mulhi(w, m31), 0x44444444u, 0x32103210u);
                     uint32_t o0, o1, o2, o3;
                     lookup4(PL, sa, ca, o0, o1);
                     lookup4(PL, mulhi(sa, m16), mulhi(ca, m16), o2, o3);
-                    sts128(wrow + (((wi ^ nl) & 7) << 4), o0, o1, o2, o3);
+                    sts128(wrow + ((((col0 / 8 + wi) ^ nl) & 7) << 4), o0, o1, o2, o3);
                 }
                 if (outl) {
-                    const int c = k0 / p.chunk_m;
-                    if (j > 0 && j % ksteps_per_chunk == 0) {  // entering chunk c: rotate the windows
-                        ob = oe;
-                        oe = one;
-                        one = c + 2 <= p.ncsr ? __ldg(orow + c + 2) : oe;
+                    if constexpr (PREPACKED) {
+                        const uint32_t kend = (uint32_t)min(k0 + kBK, p.K);
+                        while (true) {  // sorted: nothing below k0 is left
+                            uint32_t rec = wc[0];
 #pragma unroll
-                        for (int e = 0; e < kWin; ++e) {
-                            wc[e] = nc[e];
-                            wv[e] = nvv[e];
+                            for (int e = 1; e < kStream; ++e)
+                                if (head == e) rec = wc[e];
+                            if ((rec & 0xFFFFu) >= kend) break;
+                            const int kl = (int)(rec & 0xFFFFu) - k0 - col0;
+                            if ((uint32_t)kl < (uint32_t)kColsT) patch(wrow, kl + col0, rec >> 16);
+                            if (++head == kStream) {
+                                head = 0;
+#pragma unroll
+                                for (int e = 0; e < kStream; ++e) wc[e] = nc[e];
+#pragma unroll
+                                for (int e = 0; e < kStream; ++e) pull(nc[e]);
+                            }
                         }
-                        load_win(oe, nc, nvv);
-                    }
-                    // columns of this step relative to what the entries store
-                    const int cbase = PREPACKED ? k0 : k0 - c * p.chunk_m;
+                    } else {
+                        if (chunk_left == 0) {  // entering the next chunk: rotate the windows
+                            ++chunk;
+                            chunk_left = ksteps_per_chunk;
+                            ob = oe;
+                            oe = one;
+                            one = chunk + 2 <= p.ncsr ? __ldg(orow + chunk + 2) : oe;
 #pragma unroll
-                    for (int e = 0; e < kWin; ++e) {
-                        const int kl = (int)wc[e] - cbase;
-                        if (ob + e < oe && kl >= 0 && kl < kBK) patch(wrow, kl, wv[e]);
-                    }
-                    for (int i = ob + kWin; i < oe; ++i) {  // rows with more than kWin outliers in this chunk
-                        const int kl = (int)__ldg(p.ccols + i) - cbase;
-                        if (kl >= 0 && kl < kBK)
-                            patch(wrow, kl,
-                                  PREPACKED ? __float_as_uint(__ldg(reinterpret_cast<const float*>(p.cvals) + i))
-                                            : (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i));
+                            for (int e = 0; e < kWin; ++e) {
+                                wc[e] = nc[e];
+                                wv[e] = nvv[e];
+                            }
+                            load_win(oe, nc, nvv);
+                        }
+                        --chunk_left;
+                        // this thread's columns in the chunk-local numbering
+                        const int cbase = k0 - chunk * p.chunk_m + col0;
+                        uint32_t hits = 0;
+#pragma unroll
+                        for (int e = 0; e < kWin; ++e)
+                            hits |= (ob + e < oe && (uint32_t)((int)wc[e] - cbase) < (uint32_t)kColsT) ? 1u << e : 0u;
+                        while (hits) {
+                            const int e = __ffs(hits) - 1;
+                            hits &= hits - 1;
+                            uint32_t cw = wc[0], vw = wv[0];
+#pragma unroll
+                            for (int q = 1; q < kWin; ++q)
+                                if (q == e) {
+                                    cw = wc[q];
+                                    vw = wv[q];
+                                }
+                            patch(wrow, (int)cw - cbase + col0, vw);
+                        }
+                        for (int i = ob + kWin; i < oe; ++i) {  // more than kWin outliers in this chunk
+                            const int kl = (int)__ldg(reinterpret_cast<const uint16_t*>(p.ccols) + i) - cbase;
+                            if ((uint32_t)kl < (uint32_t)kColsT)
+                                patch(wrow, kl + col0, (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i));
+                        }
                     }
                 }
             } else {
-                // low-rank step: X <- s * H (tokens x r), W <- B (rows x r), zero past r
+                // low-rank step: X <- s * H (tokens x r), W <- B (rows x r), zero
+                // past r; this thread writes its kWordsT 16-byte chunks of its rows
                 const int j0 = (j - p.ksteps) * kBK;
 #pragma unroll 1
                 for (int a = 0; a < NACC; ++a) {
-                    const int m = m0 + a * kTileM + td;
-                    const uint32_t xrow = st + a * P::kX + td * 128;
+                    const int m = m0 + a * kTileM + nl;
+                    const uint32_t xrow = st + a * P::kX + nl * 128;
 #pragma unroll 1
-                    for (int ch = 0; ch < 8; ++ch) {
+                    for (int ch = col0 / 8; ch < col0 / 8 + kWordsT; ++ch) {
                         float f[8];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) {
                             const int jj = j0 + 8 * ch + e;
                             f[e] = (m < p.M && jj < p.r) ? p.scale * __ldg(p.lorah + (int64_t)m * p.r + jj) : 0.f;
                         }
-                        sts128(xrow + (((ch ^ td) & 7) << 4), pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
+                        sts128(xrow + (((ch ^ nl) & 7) << 4), pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
                                pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
                     }
                 }
 #pragma unroll 1
-                for (int ch = 0; ch < 8; ++ch) {
+                for (int ch = col0 / 8; ch < col0 / 8 + kWordsT; ++ch) {
                     float f[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
@@ -356,15 +417,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
 
         // ------------------------------------------------------------ epilogue
+        // warp w reads TMEM lanes 32 (w % 4) .. +31; the kTpr warps of a
+        // lane quarter split the tile's columns
         if (!mbar_wait(acc_bar, 0)) ok = false;
         tc_fence_after_sync();
-        const int qd = warp & 3;  // TMEM lanes 32*qd .. 32*qd+31 belong to this warp
+        const int qd = warp & 3;
+        constexpr int kCcPerWarp = kBN / 32 / kTpr;
+        const int c_lo = ((warp - 2) >> 2) * kCcPerWarp;
         T* out = reinterpret_cast<T*>(p.out);
 #pragma unroll
         for (int a = 0; a < NACC; ++a) {
             const int m = m0 + a * kTileM + 32 * qd + lane;
 #pragma unroll 1
-            for (int cc = 0; cc < kBN / 32; ++cc) {
+            for (int cc = c_lo; cc < c_lo + kCcPerWarp; ++cc) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * qd) << 16) + a * kBN + 32 * cc, v);
                 tmem_ld_wait();
@@ -438,7 +503,7 @@ int launch_tiles(const GemmParams& p, cudaStream_t stream) {
     auto kern = gemm_kernel<T, NACC, NPG, PREPACKED>;
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P::kAlloc);
     if (e != cudaSuccess) return check_cuda(e, "gemm_kernel smem attribute");
-    const dim3 grid((unsigned)((p.N + kBN - 1) / kBN), (unsigned)((p.M + NACC * kTileM - 1) / (NACC * kTileM)));
+    const dim3 grid((unsigned)(((p.N + kBN - 1) / kBN) * ((p.M + NACC * kTileM - 1) / (NACC * kTileM))));
     kern<<<grid, kThreads, P::kAlloc, stream>>>(p);
     return check_cuda(cudaGetLastError(), "gemm_kernel launch");
 }

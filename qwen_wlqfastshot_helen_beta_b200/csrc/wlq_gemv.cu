@@ -50,8 +50,8 @@ struct GemvParams {
     const void* x;
     void* out;
     const int32_t* off;
-    const uint16_t* ccols;
-    const uint8_t* cvals;
+    const void* ccols;  // uint16 chunk-local columns, or uint32 records (prepacked)
+    const void* cvals;  // e5m2 bytes, or float32 corrections (prepacked)
     const uint16_t* loraB;
     const float* lorah;
     const uint16_t* gamma;
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int i = i0 + 2 * u;
-                    col[u] = i < ib ? (int)__ldg(p.ccols + i) : -1;
+                    col[u] = i < ib ? (int)(__ldg(reinterpret_cast<const uint32_t*>(p.ccols) + i) & 0xFFFFu) : -1;
                     d[u] = i < ib ? __ldg(dl + i) : 0.f;
                 }
 #pragma unroll
@@ -334,12 +334,13 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
             const int ib = __ldg(ro + cc_hi + 1);
             for (int i = __ldg(ro + cc) + (lane >> 4); i < ib; i += 2) {
                 while (i >= bound) bound = __ldg(ro + (++cc) + 1);  // entries are chunk-ordered
-                const int col = cc * p.chunk_m + (int)__ldg(p.ccols + i);
+                const int col = cc * p.chunk_m + (int)__ldg(reinterpret_cast<const uint16_t*>(p.ccols) + i);
                 if (col < kb || col >= ke) continue;
                 const uint32_t sym = (__ldg(p.q + (int64_t)row * p.wpr + (col >> 3)) >> (4 * (col & 7))) & 15u;
                 const int grp = GROUPED ? ((col + p.goff) >> p.log2G) : 0;
                 const float wl = codebook_value<T, PREPACKED>(p.lut, (int64_t)row * p.ngroups + grp, sym);
-                const float d = f16_bits_to_f32(fp8_byte_to_f16_bits(__ldg(p.cvals + i))) - wl;
+                const float d =
+                    f16_bits_to_f32(fp8_byte_to_f16_bits(__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i))) - wl;
 #pragma unroll
                 for (int m = 0; m < MT; ++m)
                     if (m < p.M) os[m] += d * x_at(m, col);

@@ -20,8 +20,8 @@ struct LinearArgs {
     const void* x;           // [M, K] act dtype
     void* out;               // [M, N] act dtype
     const int32_t* off;      // [N, ncsr + 1] or null
-    const uint16_t* ccols;   // [nnz] or null
-    const uint8_t* cvals;    // [nnz] or null
+    const void* ccols;       // [nnz] uint16 columns, or uint32 records when prepacked; or null
+    const void* cvals;       // [nnz] e5m2 bytes, or float32 corrections when prepacked; or null
     const uint16_t* loraB;   // fp16 [N, r] or null
     const float* lorah;      // fp32 [M, r] or null
     const uint16_t* gamma;   // fp16 [N] or null
@@ -42,7 +42,7 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream);
 int launch_gemm(const LinearArgs& a, cudaStream_t stream);
 int launch_prepack_outliers(const uint32_t* q, const uint16_t* lut, const int32_t* off, const uint16_t* ccols,
                             const uint8_t* cvals, int N, int K, int wpr, int group_size, int goff, int ngroups,
-                            int chunk_m, int ncsr, int dtype, uint16_t* gcols, float* delta, cudaStream_t stream);
+                            int chunk_m, int ncsr, int dtype, uint32_t* recs, float* delta, cudaStream_t stream);
 int launch_prepack_lut(const uint16_t* in, uint32_t* out, int64_t n, int dtype, cudaStream_t stream);
 int launch_dequant(const uint32_t* q, const uint16_t* lut, uint16_t* W, const int32_t* off,
                    const uint16_t* ccols, const uint8_t* cvals, int N, int K, int bits, int wpr,

@@ -269,3 +269,42 @@ def test_errors_are_raised():
     with pytest.raises(RuntimeError, match="multiple of 32"):
         C().gemm_forward(x, T["q"], torch.zeros(32 * 3 * 16, dtype=torch.float16, device="cuda"), out, 32, 256, 4,
                          L.wpr, None, None, None, lut_group_size=128, lut_group_offset=16)
+
+
+def test_prepack_outlier_records():
+    """wlq_prepack_outliers: per entry a record (global column | outlier value
+    in the MMA type << 16) and the correction outlier - codebook value; rows
+    reordered by ascending column, also when a chunk lists its entries in
+    reverse."""
+    rng = np.random.default_rng(31)
+    N, K, G, goff = 24, 1500, 128, 64
+    L = make_np_layer(rng, N, K, G, goff, density=0.03)
+    cols_rev, vals_rev = L.cols.copy(), L.vals.copy()  # every chunk reversed: still a valid chunk-CSR
+    for r in range(N):
+        for c in range(L.off.shape[1] - 1):
+            a, b = L.off[r, c], L.off[r, c + 1]
+            cols_rev[a:b] = L.cols[a:b][::-1]
+            vals_rev[a:b] = L.vals[a:b][::-1]
+    Wcb = O.dequant(L.q, L.wpr, L.lut, N, K, 4, G, goff)  # codebook values, no outliers
+    d = "cuda"
+    q = torch.from_numpy(L.q.view(np.int32)).to(d)
+    lut = torch.from_numpy(np.ascontiguousarray(L.lut)).to(d)
+    off = torch.from_numpy(L.off).to(d)
+    for dtype in (torch.float16, torch.bfloat16):
+        for cols, vals in ((L.cols, L.vals), (cols_rev, vals_rev)):
+            rec, delta = C().prepack_outliers(q, lut, off, torch.from_numpy(cols.astype(np.uint16)).to(d),
+                                              torch.from_numpy(vals).to(d), N, K, 4, dtype, G, goff)
+            rec = rec.cpu().numpy().view(np.uint32)
+            delta = delta.cpu().numpy()
+            for r in range(N):
+                a, b = L.off[r, 0], L.off[r, -1]
+                gcol = (rec[a:b] & 0xFFFF).astype(np.int64)
+                chunk = np.repeat(np.arange(L.off.shape[1] - 1), np.diff(L.off[r]))
+                ref_cols = chunk * 512 + L.cols[a:b].astype(np.int64)
+                order = np.argsort(ref_cols, kind="stable")
+                assert np.array_equal(gcol, ref_cols[order]), r  # ascending, same set
+                ov = torch.from_numpy(O.fp8_bytes_to_fp16(L.vals[a:b][order])).to(dtype)
+                vbits = ov.view(torch.int16).numpy().view(np.uint16).astype(np.uint32)
+                assert np.array_equal(rec[a:b] >> 16, vbits), r
+                cb = torch.from_numpy(Wcb[r, gcol]).to(dtype).float().numpy()
+                assert np.array_equal(delta[a:b], ov.float().numpy() - cb), r
