@@ -6,10 +6,12 @@
 // materialises the whole dequantised weight in HBM before a cuBLAS GEMM.
 //
 // One CTA computes a (NACC x 128) x 128 tile of out = gamma * (X W^T + s H B^T):
-//   warp 0      TMA producer: X tiles (64 k x 128 tokens, 128-byte swizzle),
-//               the 128 x 64 index tile and its codebooks, per pipeline stage;
+//   warp 0      TMA producer of the activation tiles (64 k x 128 tokens,
+//               128-byte swizzle);
 //   warp 1      allocates TMEM and issues tcgen05.mma from one thread;
-//   warps 2..9  two threads per weight row: LUT lookups in registers (byte
+//   warp 2      TMA producer of the 128 x 64 index tiles and their codebooks
+//               (a deep ring of its own, so dequantisation never waits on it);
+//   warps 3..18 four threads per weight row: LUT lookups in registers (byte
 //               permutes, as in the decode GEMV) written as the K-major
 //               128-byte-swizzled bf16/f16 tile the MMA reads, outlier values
 //               patched in, then the epilogue (TMEM -> gamma -> global).
@@ -34,16 +36,14 @@ namespace {
 constexpr int kBK = 64;           // k per stage: one 128-byte swizzle row of 16-bit values
 constexpr int kBN = 128;          // weight rows (output features) per CTA
 constexpr int kTileM = 128;       // tokens per accumulator (MMA M)
-#ifndef WLQ_GEMM_TPR
-#define WLQ_GEMM_TPR 4
-#endif
-constexpr int kTpr = WLQ_GEMM_TPR;   // dequant threads per weight row
-constexpr int kDeq = 128 * kTpr;     // dequant / epilogue threads (warps 2 ..)
-constexpr int kColsT = kBK / kTpr;   // columns of a step per dequant thread (<= 32: one codebook group)
+constexpr int kTpr = 4;           // dequant threads per weight row
+constexpr int kDeq = 128 * kTpr;  // dequant / epilogue threads (warps 3 ..)
+constexpr int kDeqWarps = kDeq / 32;
+constexpr int kColsT = kBK / kTpr;   // columns of a step per dequant thread (one codebook group)
 constexpr int kWordsT = kColsT / 8;  // index words per dequant thread
-constexpr int kThreads = 64 + kDeq;
+constexpr int kDeqBase = 96;      // warps 0..2: activation producer, MMA, index producer
+constexpr int kThreads = kDeqBase + kDeq;
 constexpr int kWin = 8;           // reference layout: outliers per (row, chunk) held in registers
-constexpr int kStream = 4;        // prepacked layout: sorted outliers per row held in registers
 constexpr int kSmemLimit = 227 * 1024;
 
 struct GemmParams {
@@ -66,23 +66,37 @@ struct GemmParams {
     int vec_out;         // rows of out are 16-byte aligned
 };
 
-// Shared-memory plan of one CTA: kStages stages of [X tiles | W tile | index
-// tile | codebooks], each 1024-byte aligned (the swizzle atom), then the
-// mbarriers, the TMEM address and gamma.
+// Shared-memory plan of one CTA: three rings, each slot 1024-byte aligned
+// (the swizzle atom): activation tiles (SX slots, filled by TMA, freed by the
+// MMAs), weight tiles (SW slots, written by the dequant threads, freed by the
+// MMAs) and index/codebook tiles (SI slots, filled by TMA, freed by the
+// dequant threads).  The last ring is small per slot and deep, so the
+// dequant inputs arrive long before they are needed; then the mbarriers, the
+// TMEM address and gamma.
 template <int NACC, int NPG>
 struct Plan {
-    static constexpr int kX = kTileM * kBK * 2;  // one accumulator's X tile
-    static constexpr int kWoff = NACC * kX;
-    static constexpr int kIdxOff = kWoff + kBN * kBK * 2;
-    static constexpr int kPlOff = kIdxOff + kBN * 32;
-    static constexpr int kStage = (kPlOff + kBN * 32 * NPG + 1023) / 1024 * 1024;
-    static constexpr int kTail = 1024;  // barriers, TMEM slot, gamma
-    static constexpr int kStages = (kSmemLimit - 1024 - kTail) / kStage > 6 ? 6 : (kSmemLimit - 1024 - kTail) / kStage;
-    static constexpr int kBarOff = kStages * kStage;
+    static constexpr int kX = kTileM * kBK * 2;          // one accumulator's activation tile
+    static constexpr int kXStage = NACC * kX;
+    static constexpr int kWStage = kBN * kBK * 2;
+    static constexpr int kIdx = kBN * 32;                  // 128 rows x 8 index words
+    static constexpr int kTma = kIdx + kBN * 32 * NPG;     // + codebooks: the bytes TMA lands
+    static constexpr int kIStage = kTma;
+    // activation tiles take ~2500 cycles to land (L2), so their ring is the
+    // deepest that fits; the index ring is consumed at the dequant pace and
+    // gets what is left (at least 2 slots)
+    static constexpr int kSX = NACC == 2 ? 4 : 6;
+    static constexpr int kSW = (NACC == 2 && NPG == 2) ? 3 : 4;
+    static constexpr int kBudget = kSmemLimit - 2048;
+    static constexpr int kSIfit = (kBudget - kSX * kXStage - kSW * kWStage) / kIStage;
+    static constexpr int kSI = kSIfit > 8 ? 8 : kSIfit;
+    static constexpr int kXOff = 0;
+    static constexpr int kWOff = kSX * kXStage;
+    static constexpr int kIOff = kWOff + kSW * kWStage;
+    static constexpr int kBarOff = kIOff + kSI * kIStage;
     static constexpr int kGammaOff = kBarOff + 512;
-    static constexpr int kAlloc = kBarOff + kTail + 1024;  // + alignment slack
-    static constexpr uint32_t kTx = NACC * kX + kBN * 32 + kBN * 32 * NPG;
-    static_assert(kStages >= 2, "shared memory too small for a pipeline");
+    static constexpr int kAlloc = kBarOff + 1024 + 1024;  // barriers + gamma, alignment slack
+    static_assert(kSI >= 2, "shared memory too small for the index ring");
+    static_assert(kTma % 1024 == 0, "slots stay 1024-byte aligned");
 };
 
 __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
@@ -118,18 +132,24 @@ template <typename T, int NACC, int NPG, bool PREPACKED>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
     using P = Plan<NACC, NPG>;
     constexpr bool GROUPED = NPG > 0;
-    constexpr int S = P::kStages;
+    constexpr int SX = P::kSX, SW = P::kSW, SI = P::kSI;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t sb = (raw + 1023u) & ~1023u;
     uint8_t* sgen = smem_raw + (sb - raw);
     const uint32_t bars = sb + P::kBarOff;
-    auto full_bar = [&](int s) { return bars + 8u * s; };            // TMA landed (or stage handed over)
-    auto wfull_bar = [&](int s) { return bars + 8u * (S + s); };     // operand tiles written by threads
-    auto empty_bar = [&](int s) { return bars + 8u * (2 * S + s); }; // MMAs reading the stage are done
-    const uint32_t acc_bar = bars + 8u * (3 * S);
-    const uint32_t tmem_slot = bars + 8u * (3 * S + 1);
+    auto xfull = [&](int s) { return bars + 8u * s; };                    // activations landed / slot handed over
+    auto xempty = [&](int s) { return bars + 8u * (SX + s); };            // MMAs done with the slot
+    auto wfull = [&](int s) { return bars + 8u * (2 * SX + s); };         // weight tile written
+    auto wempty = [&](int s) { return bars + 8u * (2 * SX + SW + s); };   // MMAs done with the slot
+    auto ifull = [&](int s) { return bars + 8u * (2 * SX + 2 * SW + s); };           // index tile landed
+    auto iempty = [&](int s) { return bars + 8u * (2 * SX + 2 * SW + SI + s); };     // dequant done with it
+    const uint32_t acc_bar = bars + 8u * (2 * SX + 2 * SW + 2 * SI);
+    const uint32_t tmem_slot = acc_bar + 8u;
     float* gam = reinterpret_cast<float*>(sgen + P::kGammaOff);
+    auto xslot = [&](int s) { return sb + P::kXOff + s * P::kXStage; };
+    auto wslot = [&](int s) { return sb + P::kWOff + s * P::kWStage; };
+    auto islot = [&](int s) { return sb + P::kIOff + s * P::kIStage; };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -142,10 +162,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const bool dora = p.r > 0;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(wfull_bar(s), kDeq);
-            mbar_init(empty_bar(s), 1);
+        for (int s = 0; s < SX; ++s) {
+            mbar_init(xfull(s), 1);
+            mbar_init(xempty(s), 1);
+        }
+        for (int s = 0; s < SW; ++s) {
+            mbar_init(wfull(s), kDeqWarps);
+            mbar_init(wempty(s), 1);
+        }
+        for (int s = 0; s < SI; ++s) {
+            mbar_init(ifull(s), 1);
+            mbar_init(iempty(s), kDeqWarps);
         }
         mbar_init(acc_bar, 1);
         mbar_fence_init();
@@ -157,68 +184,80 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         tmem_alloc(tmem_slot, NACC * kBN);
         tmem_relinquish();
     }
-    if (threadIdx.x >= 64 && threadIdx.x < 64 + kBN) {
-        const int n = n0 + threadIdx.x - 64;
-        gam[threadIdx.x - 64] = (dora && n < p.N) ? f16_bits_to_f32(__ldg(p.gamma + n)) : 1.f;
+    if (threadIdx.x >= kDeqBase && threadIdx.x < kDeqBase + kBN) {
+        const int n = n0 + threadIdx.x - kDeqBase;
+        gam[threadIdx.x - kDeqBase] = (dora && n < p.N) ? f16_bits_to_f32(__ldg(p.gamma + n)) : 1.f;
     }
     tc_fence_before_sync();
     __syncthreads();
     tc_fence_after_sync();
-    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sgen + P::kBarOff + 8 * (3 * S + 1));
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sgen + P::kBarOff + (tmem_slot - bars));
 
     auto group_at = [&](int col) { return min((col + p.goff) >> p.log2G, p.ngroups - 1); };
 
     if (warp == 0) {
-        // ------------------------------------------------------------ producer
+        // ------------------------------------------------ activation producer
         if (lane == 0) {
             int issued = 0;
             for (int j = 0; j < steps; ++j) {
-                const int s = j % S, u = j / S;
-                if (u > 0 && !mbar_wait(empty_bar(s), (u - 1) & 1)) break;
+                const int s = j % SX, u = j / SX;
+                if (u > 0 && !mbar_wait(xempty(s), (u - 1) & 1)) break;
                 issued = j + 1;
-                const uint32_t st = sb + s * P::kStage;
                 if (j < p.ksteps) {
-                    mbar_arrive_expect_tx(full_bar(s), P::kTx);
+                    mbar_arrive_expect_tx(xfull(s), (uint32_t)P::kXStage);
 #pragma unroll
                     for (int a = 0; a < NACC; ++a)
-                        tma_load_2d(st + a * P::kX, &p.tm_x, full_bar(s), j * kBK, m0 + a * kTileM);
-                    tma_load_2d(st + P::kIdxOff, &p.tm_q, full_bar(s), j * (kBK / 8), n0);
-                    if constexpr (GROUPED) tma_load_2d(st + P::kPlOff, &p.tm_lut, full_bar(s), group_at(j * kBK) * 8, n0);
+                        tma_load_2d(xslot(s) + a * P::kX, &p.tm_x, xfull(s), j * kBK, m0 + a * kTileM);
                 } else {
-                    mbar_arrive(full_bar(s));  // low-rank step: the dequant threads fill both operands
+                    mbar_arrive(xfull(s));  // low-rank step: the dequant threads write the slot
                 }
             }
             // no copy may still be landing when the CTA exits (matters only
-            // after a wait ran out): the last use of each stage has completed
-            for (int j = issued > S ? issued - S : 0; j < issued; ++j) mbar_wait(full_bar(j % S), (j / S) & 1);
+            // after a wait ran out): the last use of each slot has completed
+            for (int j = issued > SX ? issued - SX : 0; j < issued; ++j) mbar_wait(xfull(j % SX), (j / SX) & 1);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------- index/codebook producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int j = 0; j < p.ksteps; ++j) {
+                const int s = j % SI, u = j / SI;
+                if (u > 0 && !mbar_wait(iempty(s), (u - 1) & 1)) break;
+                issued = j + 1;
+                mbar_arrive_expect_tx(ifull(s), (uint32_t)P::kTma);
+                tma_load_2d(islot(s), &p.tm_q, ifull(s), j * (kBK / 8), n0);
+                if constexpr (GROUPED) tma_load_2d(islot(s) + P::kIdx, &p.tm_lut, ifull(s), group_at(j * kBK) * 8, n0);
+            }
+            for (int j = issued > SI ? issued - SI : 0; j < issued; ++j) mbar_wait(ifull(j % SI), (j / SI) & 1);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issue
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16(ActTraits<T>::kIsF16 ? 0u : 1u, kTileM, kBN);
             for (int j = 0; j < steps; ++j) {
-                const int s = j % S, u = j / S;
-                if (!mbar_wait(full_bar(s), u & 1) || !mbar_wait(wfull_bar(s), u & 1)) break;
+                const int sx = j % SX, sw = j % SW;
+                if (!mbar_wait(xfull(sx), (j / SX) & 1) || !mbar_wait(wfull(sw), (j / SW) & 1)) break;
                 tc_fence_after_sync();
-                const uint32_t st = sb + s * P::kStage;
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk) {
-                    const uint64_t bdesc = umma_desc_sw128(st + P::kWoff + kk * 32);
+                    const uint64_t bdesc = umma_desc_sw128(wslot(sw) + kk * 32);
 #pragma unroll
                     for (int a = 0; a < NACC; ++a)
-                        umma_f16(tmem + a * kBN, umma_desc_sw128(st + a * P::kX + kk * 32), bdesc, idesc,
+                        umma_f16(tmem + a * kBN, umma_desc_sw128(xslot(sx) + a * P::kX + kk * 32), bdesc, idesc,
                                  (j | kk) != 0);
                 }
-                umma_commit(empty_bar(s));
+                umma_commit(xempty(sx));
+                umma_commit(wempty(sw));
             }
             umma_commit(acc_bar);  // completes once every issued MMA has
         }
     } else {
         // ------------------------------------------------------- dequant rows
-        // kTpr threads per weight row: thread (nl, part) owns columns
-        // [kColsT part, kColsT part + kColsT) of every step (kWordsT index
-        // words, one codebook: groups are >= 32 columns and 32-aligned)
-        const int td = threadIdx.x - 64;
+        // kTpr threads per weight row, the row's threads adjacent lanes of
+        // one warp: thread (nl, part) owns columns [kColsT part, +kColsT) of
+        // every step (kWordsT index words, one codebook: groups are >= 32
+        // columns and 32-aligned)
+        const int td = threadIdx.x - kDeqBase;
         const int nl = td / kTpr;
         const int part = td % kTpr;
         const int col0 = kColsT * part;
@@ -230,18 +269,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         LutPlanes PR;  // per-row codebook (ungrouped)
         if (!GROUPED) load_planes<T, PREPACKED>(p.lut, n, nv, PR);
 
-        // outliers of this row.  Prepacked layout: the row's entries are
-        // sorted by global column and stream through two kStream-entry
-        // register windows: entries are consumed from the current one by
-        // index, and the other, loaded a whole window earlier, replaces it
-        // when it runs out (no read waits on a load just issued).  Reference
-        // layout: the first kWin entries of the current chunk in registers,
-        // the next chunk's prefetched one chunk ahead.
+        // outliers of this row.  Prepacked layout: the row's records are
+        // sorted by column; each of the row's threads keeps the next three in
+        // registers (x0 next), so a step without an outlier costs one compare,
+        // and a consumed record is replaced by one loaded two consumptions
+        // earlier.  Reference layout: each thread keeps the first kWin entries
+        // of the current chunk in registers, the next chunk's prefetched one
+        // chunk ahead.
         const bool outl = p.off != nullptr && nv;
         const int32_t* orow = p.off + (int64_t)(nv ? n : 0) * (p.ncsr + 1);
-        int ob = 0, oe = 0, one = 0, row_end = 0, li = 0;
+        int ob = 0, oe = 0, one = 0, row_end = 0;
         uint32_t wc[kWin], wv[kWin], nc[kWin], nvv[kWin];
-        int head = 0;  // prepacked: next entry of window wc/wv
+        const uint32_t* recs = reinterpret_cast<const uint32_t*>(p.ccols);
+        auto ld_rec = [&](int i) { return i < row_end ? __ldg(recs + i) : 0xFFFFu; };  // 0xFFFF: none (K <= 65535)
+        uint32_t x0 = 0xFFFFu, x1 = 0xFFFFu, x2 = 0xFFFFu;
+        int xi = 0;  // index of x0
         auto load_win = [&](int base, uint32_t (&c)[kWin], uint32_t (&v)[kWin]) {
 #pragma unroll
             for (int e = 0; e < kWin; ++e) {
@@ -251,24 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 v[e] = in ? (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i) : 0u;
             }
         };
-        // next record of the sorted stream (column | value << 16); nothing
-        // here waits on the load (a record is first used a window later).
-        // Column 0xFFFF (an entry past K, sorted last, or the end of the row)
-        // is never below a step's end because K <= 65535.
-        auto pull = [&](uint32_t& rec) {
-            const bool in = li < row_end;
-            rec = in ? __ldg(reinterpret_cast<const uint32_t*>(p.ccols) + li) : 0xFFFFu;
-            li += in ? 1 : 0;
-        };
         if (outl) {
             row_end = __ldg(orow + p.ncsr);
             ob = __ldg(orow);
             if constexpr (PREPACKED) {
-                li = ob;
-#pragma unroll
-                for (int e = 0; e < kStream; ++e) pull(wc[e]);
-#pragma unroll
-                for (int e = 0; e < kStream; ++e) pull(nc[e]);
+                xi = ob;
+                x0 = ld_rec(xi);
+                x1 = ld_rec(xi + 1);
+                x2 = ld_rec(xi + 2);
             } else {
                 oe = __ldg(orow + 1);
                 one = p.ncsr > 1 ? __ldg(orow + 2) : oe;
@@ -290,24 +322,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         };
 
         for (int j = 0; j < steps && ok; ++j) {
-            const int s = j % S, u = j / S;
-            if (!mbar_wait(full_bar(s), u & 1)) { ok = false; break; }
-            const uint32_t st = sb + s * P::kStage;
-            const uint32_t wrow = st + P::kWoff + nl * 128;
+            const int sw = j % SW, uw = j / SW;
+            if (uw > 0 && !mbar_wait(wempty(sw), (uw - 1) & 1)) { ok = false; break; }
+            const uint32_t wrow = wslot(sw) + nl * 128;
             if (j < p.ksteps) {
+                const int si = j % SI;
+                if (!mbar_wait(ifull(si), (j / SI) & 1)) { ok = false; break; }
                 const int k0 = j * kBK;
                 uint32_t words[kWordsT];
                 if constexpr (kWordsT == 4) {
-                    const uint4 w4 = lds128(st + P::kIdxOff + nl * 32 + col0 / 2);
+                    const uint4 w4 = lds128(islot(si) + nl * 32 + col0 / 2);
                     words[0] = w4.x; words[1] = w4.y; words[2] = w4.z; words[3] = w4.w;
                 } else {
-                    const uint2 w2 = lds64(st + P::kIdxOff + nl * 32 + col0 / 2);
+                    const uint2 w2 = lds64(islot(si) + nl * 32 + col0 / 2);
                     words[0] = w2.x; words[1] = w2.y;
                 }
                 LutPlanes PL;
                 if constexpr (GROUPED) {
                     const int slot = NPG == 2 ? group_at(k0 + col0) - group_at(k0) : 0;
-                    planes_from_smem<T, PREPACKED>(st + P::kPlOff + nl * (32 * NPG) + 32 * slot, PL);
+                    planes_from_smem<T, PREPACKED>(islot(si) + P::kIdx + nl * (32 * NPG) + 32 * slot, PL);
                 } else {
                     PL = PR;
                 }
@@ -321,73 +354,71 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     lookup4(PL, mulhi(sa, m16), mulhi(ca, m16), o2, o3);
                     sts128(wrow + ((((col0 / 8 + wi) ^ nl) & 7) << 4), o0, o1, o2, o3);
                 }
-                if (outl) {
-                    if constexpr (PREPACKED) {
-                        const uint32_t kend = (uint32_t)min(k0 + kBK, p.K);
-                        while (true) {  // sorted: nothing below k0 is left
-                            uint32_t rec = wc[0];
-#pragma unroll
-                            for (int e = 1; e < kStream; ++e)
-                                if (head == e) rec = wc[e];
-                            if ((rec & 0xFFFFu) >= kend) break;
-                            const int kl = (int)(rec & 0xFFFFu) - k0 - col0;
-                            if ((uint32_t)kl < (uint32_t)kColsT) patch(wrow, kl + col0, rec >> 16);
-                            if (++head == kStream) {
-                                head = 0;
-#pragma unroll
-                                for (int e = 0; e < kStream; ++e) wc[e] = nc[e];
-#pragma unroll
-                                for (int e = 0; e < kStream; ++e) pull(nc[e]);
-                            }
-                        }
-                    } else {
-                        if (chunk_left == 0) {  // entering the next chunk: rotate the windows
-                            ++chunk;
-                            chunk_left = ksteps_per_chunk;
-                            ob = oe;
-                            oe = one;
-                            one = chunk + 2 <= p.ncsr ? __ldg(orow + chunk + 2) : oe;
-#pragma unroll
-                            for (int e = 0; e < kWin; ++e) {
-                                wc[e] = nc[e];
-                                wv[e] = nvv[e];
-                            }
-                            load_win(oe, nc, nvv);
-                        }
-                        --chunk_left;
-                        // this thread's columns in the chunk-local numbering
-                        const int cbase = k0 - chunk * p.chunk_m + col0;
-                        uint32_t hits = 0;
-#pragma unroll
-                        for (int e = 0; e < kWin; ++e)
-                            hits |= (ob + e < oe && (uint32_t)((int)wc[e] - cbase) < (uint32_t)kColsT) ? 1u << e : 0u;
-                        while (hits) {
-                            const int e = __ffs(hits) - 1;
-                            hits &= hits - 1;
-                            uint32_t cw = wc[0], vw = wv[0];
-#pragma unroll
-                            for (int q = 1; q < kWin; ++q)
-                                if (q == e) {
-                                    cw = wc[q];
-                                    vw = wv[q];
-                                }
-                            patch(wrow, (int)cw - cbase + col0, vw);
-                        }
-                        for (int i = ob + kWin; i < oe; ++i) {  // more than kWin outliers in this chunk
-                            const int kl = (int)__ldg(reinterpret_cast<const uint16_t*>(p.ccols) + i) - cbase;
-                            if ((uint32_t)kl < (uint32_t)kColsT)
-                                patch(wrow, kl + col0, (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i));
-                        }
+                if constexpr (PREPACKED) {
+                    const uint32_t kend = (uint32_t)min(k0 + kBK, p.K);
+                    while ((x0 & 0xFFFFu) < kend) {  // sorted: nothing below k0 is left
+                        const int kl = (int)(x0 & 0xFFFFu) - k0;
+                        if ((uint32_t)(kl - col0) < (uint32_t)kColsT) patch(wrow, kl, x0 >> 16);
+                        ++xi;
+                        x0 = x1;
+                        x1 = x2;
+                        x2 = ld_rec(xi + 2);
                     }
+                } else if (outl) {
+                    if (chunk_left == 0) {  // entering the next chunk: rotate the windows
+                        ++chunk;
+                        chunk_left = ksteps_per_chunk;
+                        ob = oe;
+                        oe = one;
+                        one = chunk + 2 <= p.ncsr ? __ldg(orow + chunk + 2) : oe;
+#pragma unroll
+                        for (int e = 0; e < kWin; ++e) {
+                            wc[e] = nc[e];
+                            wv[e] = nvv[e];
+                        }
+                        load_win(oe, nc, nvv);
+                    }
+                    --chunk_left;
+                    // this thread's columns in the chunk-local numbering
+                    const int cbase = k0 - chunk * p.chunk_m + col0;
+                    uint32_t hits = 0;
+#pragma unroll
+                    for (int e = 0; e < kWin; ++e)
+                        hits |= (ob + e < oe && (uint32_t)((int)wc[e] - cbase) < (uint32_t)kColsT) ? 1u << e : 0u;
+                    while (hits) {
+                        const int e = __ffs(hits) - 1;
+                        hits &= hits - 1;
+                        uint32_t cw = wc[0], vw = wv[0];
+#pragma unroll
+                        for (int q = 1; q < kWin; ++q)
+                            if (q == e) {
+                                cw = wc[q];
+                                vw = wv[q];
+                            }
+                        patch(wrow, (int)cw - cbase + col0, vw);
+                    }
+                    for (int i = ob + kWin; i < oe; ++i) {  // more than kWin outliers in this chunk
+                        const int kl = (int)__ldg(reinterpret_cast<const uint16_t*>(p.ccols) + i) - cbase;
+                        if ((uint32_t)kl < (uint32_t)kColsT)
+                            patch(wrow, kl + col0, (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i));
+                    }
+                }
+                fence_proxy_async_smem();  // generic-proxy tile writes -> tensor core
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(iempty(si));
+                    mbar_arrive(wfull(sw));
                 }
             } else {
                 // low-rank step: X <- s * H (tokens x r), W <- B (rows x r), zero
                 // past r; this thread writes its kWordsT 16-byte chunks of its rows
+                const int sx = j % SX;
+                if (!mbar_wait(xfull(sx), (j / SX) & 1)) { ok = false; break; }  // slot handed over
                 const int j0 = (j - p.ksteps) * kBK;
 #pragma unroll 1
                 for (int a = 0; a < NACC; ++a) {
                     const int m = m0 + a * kTileM + nl;
-                    const uint32_t xrow = st + a * P::kX + nl * 128;
+                    const uint32_t xrow = xslot(sx) + a * P::kX + nl * 128;
 #pragma unroll 1
                     for (int ch = col0 / 8; ch < col0 / 8 + kWordsT; ++ch) {
                         float f[8];
@@ -411,19 +442,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     sts128(wrow + (((ch ^ nl) & 7) << 4), pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
                            pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
                 }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(wfull(sw));
             }
-            fence_proxy_async_smem();  // generic-proxy tile writes -> tensor core
-            mbar_arrive(wfull_bar(s));
         }
 
         // ------------------------------------------------------------ epilogue
-        // warp w reads TMEM lanes 32 (w % 4) .. +31; the kTpr warps of a
-        // lane quarter split the tile's columns
+        // warp w reads TMEM lanes 32 (w % 4) .. +31; the kTpr warps of a lane
+        // quarter split the tile's columns
         if (!mbar_wait(acc_bar, 0)) ok = false;
         tc_fence_after_sync();
         const int qd = warp & 3;
         constexpr int kCcPerWarp = kBN / 32 / kTpr;
-        const int c_lo = ((warp - 2) >> 2) * kCcPerWarp;
+        const int c_lo = ((warp - kDeqBase / 32) >> 2) * kCcPerWarp;
         T* out = reinterpret_cast<T*>(p.out);
 #pragma unroll
         for (int a = 0; a < NACC; ++a) {
