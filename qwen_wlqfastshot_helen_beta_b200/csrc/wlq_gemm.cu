@@ -34,13 +34,21 @@ namespace wlq {
 namespace {
 
 constexpr int kBK = 64;           // k per stage: one 128-byte swizzle row of 16-bit values
-constexpr int kBN = 128;          // weight rows (output features) per CTA
 constexpr int kTileM = 128;       // tokens per accumulator (MMA M)
-constexpr int kTpr = 4;           // dequant threads per weight row
-constexpr int kDeq = 128 * kTpr;  // dequant / epilogue threads (warps 3 ..)
+constexpr int kDeq = 512;         // dequant / epilogue threads (warps 3 ..)
 constexpr int kDeqWarps = kDeq / 32;
-constexpr int kColsT = kBK / kTpr;   // columns of a step per dequant thread (one codebook group)
-constexpr int kWordsT = kColsT / 8;  // index words per dequant thread
+
+// Work split for a tile of BN weight rows (128 or 256) over the kDeq dequant
+// threads: kTpr threads per row, kColsT columns of a step each (at most 32:
+// one codebook group), epilogue column chunks per warp and accumulator.
+template <int BN>
+struct Tile {
+    static constexpr int kTpr = kDeq / BN;
+    static constexpr int kColsT = kBK / kTpr;
+    static constexpr int kWordsT = kColsT / 8;
+    static constexpr int kCcPerWarp = BN / 32 / (kDeqWarps / 4);
+    static_assert(kColsT <= 32 && kWordsT >= 1, "one codebook group per thread and step");
+};
 constexpr int kDeqBase = 96;      // warps 0..2: activation producer, MMA, index producer
 constexpr int kThreads = kDeqBase + kDeq;
 constexpr int kWin = 8;           // reference layout: outliers per (row, chunk) held in registers
@@ -73,19 +81,19 @@ struct GemmParams {
 // dequant threads).  The last ring is small per slot and deep, so the
 // dequant inputs arrive long before they are needed; then the mbarriers, the
 // TMEM address and gamma.
-template <int NACC, int NPG>
+template <int NACC, int NPG, int BN>
 struct Plan {
     static constexpr int kX = kTileM * kBK * 2;          // one accumulator's activation tile
     static constexpr int kXStage = NACC * kX;
-    static constexpr int kWStage = kBN * kBK * 2;
-    static constexpr int kIdx = kBN * 32;                  // 128 rows x 8 index words
-    static constexpr int kTma = kIdx + kBN * 32 * NPG;     // + codebooks: the bytes TMA lands
+    static constexpr int kWStage = BN * kBK * 2;
+    static constexpr int kIdx = BN * 32;                   // BN rows x 8 index words
+    static constexpr int kTma = kIdx + BN * 32 * NPG;      // + codebooks: the bytes TMA lands
     static constexpr int kIStage = kTma;
     // activation tiles take ~2500 cycles to land (L2), so their ring is the
     // deepest that fits; the index ring is consumed at the dequant pace and
     // gets what is left (at least 2 slots)
-    static constexpr int kSX = NACC == 2 ? 4 : 6;
-    static constexpr int kSW = (NACC == 2 && NPG == 2) ? 3 : 4;
+    static constexpr int kSX = BN == 256 ? 3 : (NACC == 2 ? 4 : 6);
+    static constexpr int kSW = BN == 256 ? (NPG == 2 ? 2 : 3) : ((NACC == 2 && NPG == 2) ? 3 : 4);
     static constexpr int kBudget = kSmemLimit - 2048;
     static constexpr int kSIfit = (kBudget - kSX * kXStage - kSW * kWStage) / kIStage;
     static constexpr int kSI = kSIfit > 8 ? 8 : kSIfit;
@@ -94,7 +102,7 @@ struct Plan {
     static constexpr int kIOff = kWOff + kSW * kWStage;
     static constexpr int kBarOff = kIOff + kSI * kIStage;
     static constexpr int kGammaOff = kBarOff + 512;
-    static constexpr int kAlloc = kBarOff + 1024 + 1024;  // barriers + gamma, alignment slack
+    static constexpr int kAlloc = kGammaOff + 4 * BN + 1024;  // barriers + gamma, alignment slack
     static_assert(kSI >= 2, "shared memory too small for the index ring");
     static_assert(kTma % 1024 == 0, "slots stay 1024-byte aligned");
 };
@@ -128,9 +136,10 @@ __device__ __forceinline__ uint32_t sw128_elem(uint32_t row_addr, int row, int k
     return row_addr + ((((k >> 3) ^ row) & 7) << 4) + ((k & 7) << 1);
 }
 
-template <typename T, int NACC, int NPG, bool PREPACKED>
+template <typename T, int NACC, int NPG, bool PREPACKED, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
-    using P = Plan<NACC, NPG>;
+    using P = Plan<NACC, NPG, BN>;
+    constexpr int kTpr = Tile<BN>::kTpr, kColsT = Tile<BN>::kColsT, kWordsT = Tile<BN>::kWordsT;
     constexpr bool GROUPED = NPG > 0;
     constexpr int SX = P::kSX, SW = P::kSW, SI = P::kSI;
     extern __shared__ uint8_t smem_raw[];
@@ -156,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     // token tiles vary fastest across the launch, so the CTAs resident at
     // one time read several activation tiles instead of all hitting one
     const int mtiles = (p.M + NACC * kTileM - 1) / (NACC * kTileM);
-    const int n0 = (int)(blockIdx.x / mtiles) * kBN;
+    const int n0 = (int)(blockIdx.x / mtiles) * BN;
     const int m0 = (int)(blockIdx.x % mtiles) * (NACC * kTileM);
     const int steps = p.ksteps + p.lsteps;
     const bool dora = p.r > 0;
@@ -181,10 +190,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (GROUPED) tma_prefetch_desc(&p.tm_lut);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, NACC * kBN);
+        tmem_alloc(tmem_slot, NACC * BN);
         tmem_relinquish();
     }
-    if (threadIdx.x >= kDeqBase && threadIdx.x < kDeqBase + kBN) {
+    if (threadIdx.x >= kDeqBase && threadIdx.x < kDeqBase + BN) {
         const int n = n0 + threadIdx.x - kDeqBase;
         gam[threadIdx.x - kDeqBase] = (dora && n < p.N) ? f16_bits_to_f32(__ldg(p.gamma + n)) : 1.f;
     }
@@ -233,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issue
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_f16(ActTraits<T>::kIsF16 ? 0u : 1u, kTileM, kBN);
+            constexpr uint32_t idesc = umma_idesc_f16(ActTraits<T>::kIsF16 ? 0u : 1u, kTileM, BN);
             for (int j = 0; j < steps; ++j) {
                 const int sx = j % SX, sw = j % SW;
                 if (!mbar_wait(xfull(sx), (j / SX) & 1) || !mbar_wait(wfull(sw), (j / SW) & 1)) break;
@@ -243,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     const uint64_t bdesc = umma_desc_sw128(wslot(sw) + kk * 32);
 #pragma unroll
                     for (int a = 0; a < NACC; ++a)
-                        umma_f16(tmem + a * kBN, umma_desc_sw128(xslot(sx) + a * P::kX + kk * 32), bdesc, idesc,
+                        umma_f16(tmem + a * BN, umma_desc_sw128(xslot(sx) + a * P::kX + kk * 32), bdesc, idesc,
                                  (j | kk) != 0);
                 }
                 umma_commit(xempty(sx));
@@ -411,35 +420,34 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 }
             } else {
                 // low-rank step: X <- s * H (tokens x r), W <- B (rows x r), zero
-                // past r; this thread writes its kWordsT 16-byte chunks of its rows
+                // past r; the dequant threads share the 16-byte chunks of both
                 const int sx = j % SX;
                 if (!mbar_wait(xfull(sx), (j / SX) & 1)) { ok = false; break; }  // slot handed over
                 const int j0 = (j - p.ksteps) * kBK;
 #pragma unroll 1
-                for (int a = 0; a < NACC; ++a) {
-                    const int m = m0 + a * kTileM + nl;
-                    const uint32_t xrow = xslot(sx) + a * P::kX + nl * 128;
-#pragma unroll 1
-                    for (int ch = col0 / 8; ch < col0 / 8 + kWordsT; ++ch) {
-                        float f[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const int jj = j0 + 8 * ch + e;
-                            f[e] = (m < p.M && jj < p.r) ? p.scale * __ldg(p.lorah + (int64_t)m * p.r + jj) : 0.f;
-                        }
-                        sts128(xrow + (((ch ^ nl) & 7) << 4), pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
-                               pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
-                    }
-                }
-#pragma unroll 1
-                for (int ch = col0 / 8; ch < col0 / 8 + kWordsT; ++ch) {
+                for (int c = td; c < NACC * kTileM * 8; c += kDeq) {
+                    const int rx = c >> 3, ch = c & 7, a = rx / kTileM, rr = rx % kTileM;
+                    const int m = m0 + rx;
                     float f[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const int jj = j0 + 8 * ch + e;
-                        f[e] = (nv && jj < p.r) ? f16_bits_to_f32(__ldg(p.loraB + (int64_t)n * p.r + jj)) : 0.f;
+                        f[e] = (m < p.M && jj < p.r) ? p.scale * __ldg(p.lorah + (int64_t)m * p.r + jj) : 0.f;
                     }
-                    sts128(wrow + (((ch ^ nl) & 7) << 4), pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
+                    sts128(xslot(sx) + a * P::kX + rr * 128 + (((ch ^ rr) & 7) << 4), pack2<T>(f[0], f[1]),
+                           pack2<T>(f[2], f[3]), pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
+                }
+#pragma unroll 1
+                for (int c = td; c < BN * 8; c += kDeq) {
+                    const int rw = c >> 3, ch = c & 7;
+                    const int nw = n0 + rw;
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int jj = j0 + 8 * ch + e;
+                        f[e] = (nw < p.N && jj < p.r) ? f16_bits_to_f32(__ldg(p.loraB + (int64_t)nw * p.r + jj)) : 0.f;
+                    }
+                    sts128(wslot(sw) + rw * 128 + (((ch ^ rw) & 7) << 4), pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]),
                            pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
                 }
                 fence_proxy_async_smem();
@@ -454,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (!mbar_wait(acc_bar, 0)) ok = false;
         tc_fence_after_sync();
         const int qd = warp & 3;
-        constexpr int kCcPerWarp = kBN / 32 / kTpr;
+        constexpr int kCcPerWarp = Tile<BN>::kCcPerWarp;
         const int c_lo = ((warp - kDeqBase / 32) >> 2) * kCcPerWarp;
         T* out = reinterpret_cast<T*>(p.out);
 #pragma unroll
@@ -463,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 #pragma unroll 1
             for (int cc = c_lo; cc < c_lo + kCcPerWarp; ++cc) {
                 uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * qd) << 16) + a * kBN + 32 * cc, v);
+                tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * qd) << 16) + a * BN + 32 * cc, v);
                 tmem_ld_wait();
                 if (!ok || m >= p.M) continue;
                 const int nb = n0 + 32 * cc;
@@ -493,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     __syncthreads();
     if (warp == 1) {
         tc_fence_after_sync();
-        tmem_dealloc(tmem, NACC * kBN);
+        tmem_dealloc(tmem, NACC * BN);
     }
 }
 
@@ -529,24 +537,36 @@ int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
     return WLQ_OK;
 }
 
-template <typename T, int NACC, int NPG, bool PREPACKED>
+template <typename T, int NACC, int NPG, bool PREPACKED, int BN>
 int launch_tiles(const GemmParams& p, cudaStream_t stream) {
-    using P = Plan<NACC, NPG>;
-    auto kern = gemm_kernel<T, NACC, NPG, PREPACKED>;
+    using P = Plan<NACC, NPG, BN>;
+    auto kern = gemm_kernel<T, NACC, NPG, PREPACKED, BN>;
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P::kAlloc);
     if (e != cudaSuccess) return check_cuda(e, "gemm_kernel smem attribute");
-    const dim3 grid((unsigned)(((p.N + kBN - 1) / kBN) * ((p.M + NACC * kTileM - 1) / (NACC * kTileM))));
+    const dim3 grid((unsigned)(((p.N + BN - 1) / BN) * ((p.M + NACC * kTileM - 1) / (NACC * kTileM))));
     kern<<<grid, kThreads, P::kAlloc, stream>>>(p);
     return check_cuda(cudaGetLastError(), "gemm_kernel launch");
 }
 
-template <typename T, int NACC>
+template <typename T, int NACC, int BN>
 int dispatch_npg(const GemmParams& p, int npg, bool prepacked, cudaStream_t stream) {
     switch (npg) {
-        case 0: return prepacked ? launch_tiles<T, NACC, 0, true>(p, stream) : launch_tiles<T, NACC, 0, false>(p, stream);
-        case 1: return prepacked ? launch_tiles<T, NACC, 1, true>(p, stream) : launch_tiles<T, NACC, 1, false>(p, stream);
-        default: return prepacked ? launch_tiles<T, NACC, 2, true>(p, stream) : launch_tiles<T, NACC, 2, false>(p, stream);
+        case 0: return prepacked ? launch_tiles<T, NACC, 0, true, BN>(p, stream)
+                                 : launch_tiles<T, NACC, 0, false, BN>(p, stream);
+        case 1: return prepacked ? launch_tiles<T, NACC, 1, true, BN>(p, stream)
+                                 : launch_tiles<T, NACC, 1, false, BN>(p, stream);
+        default: return prepacked ? launch_tiles<T, NACC, 2, true, BN>(p, stream)
+                                  : launch_tiles<T, NACC, 2, false, BN>(p, stream);
     }
+}
+
+// CTA shapes built: 256 tokens x 256 or 128 rows, 128 tokens x 128 rows
+template <typename T>
+int dispatch_shape(const GemmParams& p, int nacc, int bn, int npg, bool prepacked, cudaStream_t stream) {
+    if (nacc == 2)
+        return bn == 256 ? dispatch_npg<T, 2, 256>(p, npg, prepacked, stream)
+                         : dispatch_npg<T, 2, 128>(p, npg, prepacked, stream);
+    return dispatch_npg<T, 1, 128>(p, npg, prepacked, stream);
 }
 
 // M > 16 shapes the TMA path cannot take run as decode GEMVs over 16-token slices.
@@ -580,6 +600,26 @@ int launch_gemm(const LinearArgs& a, cudaStream_t stream) {
                         (a.off == nullptr || a.chunk_m % kBK == 0);
     if (!tma_ok) return gemm_by_slices(a, stream);
 
+    // CTA shape: 256 tokens x 256 rows needs the least dequantisation and the
+    // least activation traffic per FLOP; smaller shapes fill the GPU when the
+    // problem is small.  Pick the best (relative efficiency measured on B200
+    // x fraction of the last wave that is occupied).
+    const int sms = device_sm_count();
+    struct Shape { int nacc, bn; double eff; };
+    const Shape shapes[3] = {{2, 256, 1.0}, {2, 128, 0.85}, {1, 128, 0.55}};
+    int nacc = 1, bn = 128;
+    double best = -1.0;
+    for (const Shape& sh : shapes) {
+        const int64_t tiles = ((a.N + sh.bn - 1) / sh.bn) * ((a.M + sh.nacc * kTileM - 1) / (sh.nacc * kTileM));
+        const int64_t waves = (tiles + sms - 1) / sms;
+        const double score = sh.eff * (double)tiles / (double)(waves * sms);
+        if (score > best + 1e-9) {
+            best = score;
+            nacc = sh.nacc;
+            bn = sh.bn;
+        }
+    }
+
     GemmParams p;
     memset(&p, 0, sizeof(p));
     const CUtensorMapDataType xdt =
@@ -588,14 +628,14 @@ int launch_gemm(const LinearArgs& a, cudaStream_t stream) {
                        CU_TENSOR_MAP_SWIZZLE_128B, "X");
     if (rc) return rc;
     rc = encode_2d(&p.tm_q, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.q, (uint64_t)a.wpr, (uint64_t)a.N, (uint64_t)a.wpr * 4,
-                   kBK / 8, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, "q_packed");
+                   kBK / 8, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_NONE, "q_packed");
     if (rc) return rc;
     // codebooks per 64-column step: 1 when groups of >= 64 columns align with
     // the steps, else 2 (a step then spans at most two groups)
     const int npg = a.group_size == 0 ? 0 : (a.group_size >= kBK && a.group_offset % kBK == 0) ? 1 : 2;
     if (npg > 0) {
         rc = encode_2d(&p.tm_lut, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.lut, (uint64_t)a.ngroups * 8, (uint64_t)a.N,
-                       (uint64_t)a.ngroups * 32, 8 * npg, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, "lut_c");
+                       (uint64_t)a.ngroups * 32, 8 * npg, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_NONE, "lut_c");
         if (rc) return rc;
     }
     p.lut = a.lut; p.out = a.out; p.off = a.off; p.ccols = a.ccols; p.cvals = a.cvals;
@@ -609,16 +649,8 @@ int launch_gemm(const LinearArgs& a, cudaStream_t stream) {
     p.mul31 = 1u << 31;
     p.vec_out = (a.N % 8 == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0);
 
-    // two accumulators (256 tokens per CTA) halve the dequantisation per FLOP
-    // once there are enough tiles to fill the GPU
-    const int sms = device_sm_count();
-    const int64_t ntiles = (a.N + kBN - 1) / kBN;
-    const bool two = ((int64_t)(a.M + 2 * kTileM - 1) / (2 * kTileM)) * ntiles >= sms;
-    if (a.dtype == WLQ_DTYPE_BF16)
-        return two ? dispatch_npg<__nv_bfloat16, 2>(p, npg, a.lut_prepacked, stream)
-                   : dispatch_npg<__nv_bfloat16, 1>(p, npg, a.lut_prepacked, stream);
-    return two ? dispatch_npg<__half, 2>(p, npg, a.lut_prepacked, stream)
-               : dispatch_npg<__half, 1>(p, npg, a.lut_prepacked, stream);
+    if (a.dtype == WLQ_DTYPE_BF16) return dispatch_shape<__nv_bfloat16>(p, nacc, bn, npg, a.lut_prepacked, stream);
+    return dispatch_shape<__half>(p, nacc, bn, npg, a.lut_prepacked, stream);
 }
 
 int read_device_error(int device, unsigned int* flags, int clear) {
