@@ -67,6 +67,7 @@ LAYER_CASES = [
     (48, 448, 128, 64, True, False),   # tensor-parallel shard starting mid-group
     (33, 1100, 32, 0, False, True),
     (16, 130, 0, 0, True, False),
+    (64, 18944, 128, 0, True, True),  # activations too large to stage: they stream through the ring
 ]
 
 
