@@ -283,6 +283,38 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
             }
         }
     }
+    // DoRA low-rank term s * B h on the tensor core, once per output tile
+    // (cluster rank 0): A = the tile's 16 rows of B (k = rank index), the
+    // B operand = s * h per token, both rounded to the MMA type
+    if (p.r > 0 && (gridDim.y == 1 || cluster_ctarank() == 0u)) {
+        const uint16_t* B0 = p.loraB + (int64_t)(v0 ? row0 : 0) * p.r;
+        const uint16_t* B1 = p.loraB + (int64_t)(v1 ? row0 + 8 : 0) * p.r;
+        auto bval = [&](const uint16_t* Br, bool ok, int k) -> uint32_t {  // one 16-bit element
+            return (ok && k < p.r) ? (uint32_t)ActTraits<T>::from_f16_bits(__ldg(Br + k)) : 0u;
+        };
+        for (int kb = 0; kb < p.r; kb += 16) {
+            uint32_t a[4];
+            const int k0 = kb + 2 * t, k8 = kb + 2 * t + 8;
+            a[0] = bval(B0, v0, k0) | (bval(B0, v0, k0 + 1) << 16);
+            a[1] = bval(B1, v1, k0) | (bval(B1, v1, k0 + 1) << 16);
+            a[2] = bval(B0, v0, k8) | (bval(B0, v0, k8 + 1) << 16);
+            a[3] = bval(B1, v1, k8) | (bval(B1, v1, k8 + 1) << 16);
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt) {
+                const int tok = 8 * tt + g;
+                const float* h = p.lorah + (int64_t)(tok < p.M ? tok : 0) * p.r;
+                auto hv = [&](int k) { return (tok < p.M && k < p.r) ? p.scale * __ldg(h + k) : 0.f; };
+                const T h0 = ActTraits<T>::from_f32(hv(k0)), h1 = ActTraits<T>::from_f32(hv(k0 + 1));
+                const T h8 = ActTraits<T>::from_f32(hv(k8)), h9 = ActTraits<T>::from_f32(hv(k8 + 1));
+                const uint32_t b0 = (uint32_t)*reinterpret_cast<const uint16_t*>(&h0) |
+                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(&h1) << 16);
+                const uint32_t b1 = (uint32_t)*reinterpret_cast<const uint16_t*>(&h8) |
+                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(&h9) << 16);
+                Mma16816<T>::run(acc[tt], a, b0, b1);
+            }
+        }
+    }
+
     // publish this warp's partial tile
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt)
@@ -370,13 +402,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
                 const uint32_t a = smem_u32(&part[warp][rl][tk]);
                 for (uint32_t qq = 1; qq < nranks; ++qq) s += ld_shared_cluster_f32(mapa_shared(a, qq));
             }
-            if (dora) {
-                float l = 0.f;
-                const float* h = p.lorah + (int64_t)tk * p.r;
-                const uint16_t* B = p.loraB + (int64_t)n * p.r;
-                for (int j = 0; j < p.r; ++j) l += __ldg(h + j) * f16_bits_to_f32(__ldg(B + j));
-                s = (s + p.scale * l) * f16_bits_to_f32(__ldg(p.gamma + n));
-            }
+            if (dora) s *= f16_bits_to_f32(__ldg(p.gamma + n));  // s * B h is already in s
             reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s);
         }
     }
