@@ -185,6 +185,49 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
 
+    // this row's outlier range (prepacked layout), loaded before the
+    // activation staging wait so the latency overlaps it
+    const bool o_has = p.off != nullptr && c_begin < c_end && tile_row0 + (lane & 15) < p.N;
+    int o_ia = 0, o_ib = 0;
+    if (PREPACKED && o_has) {
+        const int32_t* ro = p.off + (int64_t)(tile_row0 + (lane & 15)) * (p.ncsr + 1);
+        o_ia = __ldg(ro + c_begin * kChunk / p.chunk_m);
+        o_ib = __ldg(ro + (min(p.K, c_end * kChunk) - 1) / p.chunk_m + 1);
+    }
+
+    // DoRA low-rank term s * B h on the tensor core, once per output tile
+    // (cluster rank 0), into the accumulators before the main loop: A = the
+    // tile's 16 rows of B (k = rank index), the B operand = s * h per token,
+    // both rounded to the MMA type
+    if (p.r > 0 && (gridDim.y == 1 || cluster_ctarank() == 0u)) {
+        const uint16_t* B0 = p.loraB + (int64_t)(v0 ? row0 : 0) * p.r;
+        const uint16_t* B1 = p.loraB + (int64_t)(v1 ? row0 + 8 : 0) * p.r;
+        auto bval = [&](const uint16_t* Br, bool ok, int k) -> uint32_t {  // one 16-bit element
+            return (ok && k < p.r) ? (uint32_t)ActTraits<T>::from_f16_bits(__ldg(Br + k)) : 0u;
+        };
+        for (int kb = 0; kb < p.r; kb += 16) {
+            uint32_t a[4];
+            const int k0 = kb + 2 * t, k8 = kb + 2 * t + 8;
+            a[0] = bval(B0, v0, k0) | (bval(B0, v0, k0 + 1) << 16);
+            a[1] = bval(B1, v1, k0) | (bval(B1, v1, k0 + 1) << 16);
+            a[2] = bval(B0, v0, k8) | (bval(B0, v0, k8 + 1) << 16);
+            a[3] = bval(B1, v1, k8) | (bval(B1, v1, k8 + 1) << 16);
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt) {
+                const int tok = 8 * tt + g;
+                const float* h = p.lorah + (int64_t)(tok < p.M ? tok : 0) * p.r;
+                auto hv = [&](int k) { return (tok < p.M && k < p.r) ? p.scale * __ldg(h + k) : 0.f; };
+                const T h0 = ActTraits<T>::from_f32(hv(k0)), h1 = ActTraits<T>::from_f32(hv(k0 + 1));
+                const T h8 = ActTraits<T>::from_f32(hv(k8)), h9 = ActTraits<T>::from_f32(hv(k8 + 1));
+                const uint32_t b0 = (uint32_t)*reinterpret_cast<const uint16_t*>(&h0) |
+                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(&h1) << 16);
+                const uint32_t b1 = (uint32_t)*reinterpret_cast<const uint16_t*>(&h8) |
+                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(&h9) << 16);
+                Mma16816<T>::run(acc[tt], a, b0, b1);
+            }
+        }
+    }
+
     // this rank's activations into shared memory (XSMEM), or read through L1
     // when the slice is too large to stage
     const int kb0 = c_begin * kChunk;
@@ -225,6 +268,69 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
         return XSMEM ? ActTraits<T>::bits_to_f32(xs[m * p.x_stride + col - kb0])
                      : ActTraits<T>::to_f32(x[(int64_t)m * p.K + col]);
     };
+    // outlier replacement over this rank's K range, done before the main
+    // loop so its dependent loads overlap the ring fill instead of trailing
+    // it: lanes l and l+16 share tile row l % 16 and take alternate entries
+    // of its chunk-CSR range; the sums seed the warp's partial tile
+    {
+        const int kb = c_begin * kChunk;
+        const int ke = min(p.K, c_end * kChunk);
+        const int rl = lane & 15;
+        const int row = tile_row0 + rl;
+        float os[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) os[m] = 0.f;
+        if (PREPACKED && o_has) {
+            // global columns and ready corrections: two independent loads per
+            // entry, then the activations; four entries in flight per lane
+            const int ia = o_ia, ib = o_ib;
+            const float* dl = reinterpret_cast<const float*>(p.cvals);
+            for (int i0 = ia + (lane >> 4); i0 < ib; i0 += 8) {
+                int col[4];
+                float d[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int i = i0 + 2 * u;
+                    col[u] = i < ib ? (int)(__ldg(reinterpret_cast<const uint32_t*>(p.ccols) + i) & 0xFFFFu) : -1;
+                    d[u] = i < ib ? __ldg(dl + i) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (col[u] < kb || col[u] >= ke) continue;
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                        if (m < p.M) os[m] += d[u] * x_at(m, col[u]);
+                }
+            }
+        } else if (!PREPACKED && o_has) {
+            const int32_t* ro = p.off + (int64_t)row * (p.ncsr + 1);
+            int cc = kb / p.chunk_m;
+            const int cc_hi = (ke - 1) / p.chunk_m;
+            int bound = __ldg(ro + cc + 1);  // end of chunk cc
+            const int ib = __ldg(ro + cc_hi + 1);
+            for (int i = __ldg(ro + cc) + (lane >> 4); i < ib; i += 2) {
+                while (i >= bound) bound = __ldg(ro + (++cc) + 1);  // entries are chunk-ordered
+                const int col = cc * p.chunk_m + (int)__ldg(reinterpret_cast<const uint16_t*>(p.ccols) + i);
+                if (col < kb || col >= ke) continue;
+                const uint32_t sym = (__ldg(p.q + (int64_t)row * p.wpr + (col >> 3)) >> (4 * (col & 7))) & 15u;
+                const int grp = GROUPED ? ((col + p.goff) >> p.log2G) : 0;
+                const float wl = codebook_value<T, PREPACKED>(p.lut, (int64_t)row * p.ngroups + grp, sym);
+                const float d =
+                    f16_bits_to_f32(fp8_byte_to_f16_bits(__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i))) - wl;
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                    if (m < p.M) os[m] += d * x_at(m, col);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) os[m] += __shfl_down_sync(0xFFFFFFFFu, os[m], 16);
+        if (lane < 16) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m) part[warp][rl][m] = os[m];  // the MMA tile is added at publish
+        }
+        __syncwarp();
+    }
+
     uint4 xnext[NT];
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt) xnext[tt] = c_begin < c_end ? lds_x8(tt, 0) : make_uint4(0u, 0u, 0u, 0u);
@@ -283,109 +389,15 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
             }
         }
     }
-    // DoRA low-rank term s * B h on the tensor core, once per output tile
-    // (cluster rank 0): A = the tile's 16 rows of B (k = rank index), the
-    // B operand = s * h per token, both rounded to the MMA type
-    if (p.r > 0 && (gridDim.y == 1 || cluster_ctarank() == 0u)) {
-        const uint16_t* B0 = p.loraB + (int64_t)(v0 ? row0 : 0) * p.r;
-        const uint16_t* B1 = p.loraB + (int64_t)(v1 ? row0 + 8 : 0) * p.r;
-        auto bval = [&](const uint16_t* Br, bool ok, int k) -> uint32_t {  // one 16-bit element
-            return (ok && k < p.r) ? (uint32_t)ActTraits<T>::from_f16_bits(__ldg(Br + k)) : 0u;
-        };
-        for (int kb = 0; kb < p.r; kb += 16) {
-            uint32_t a[4];
-            const int k0 = kb + 2 * t, k8 = kb + 2 * t + 8;
-            a[0] = bval(B0, v0, k0) | (bval(B0, v0, k0 + 1) << 16);
-            a[1] = bval(B1, v1, k0) | (bval(B1, v1, k0 + 1) << 16);
-            a[2] = bval(B0, v0, k8) | (bval(B0, v0, k8 + 1) << 16);
-            a[3] = bval(B1, v1, k8) | (bval(B1, v1, k8 + 1) << 16);
-#pragma unroll
-            for (int tt = 0; tt < NT; ++tt) {
-                const int tok = 8 * tt + g;
-                const float* h = p.lorah + (int64_t)(tok < p.M ? tok : 0) * p.r;
-                auto hv = [&](int k) { return (tok < p.M && k < p.r) ? p.scale * __ldg(h + k) : 0.f; };
-                const T h0 = ActTraits<T>::from_f32(hv(k0)), h1 = ActTraits<T>::from_f32(hv(k0 + 1));
-                const T h8 = ActTraits<T>::from_f32(hv(k8)), h9 = ActTraits<T>::from_f32(hv(k8 + 1));
-                const uint32_t b0 = (uint32_t)*reinterpret_cast<const uint16_t*>(&h0) |
-                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(&h1) << 16);
-                const uint32_t b1 = (uint32_t)*reinterpret_cast<const uint16_t*>(&h8) |
-                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(&h9) << 16);
-                Mma16816<T>::run(acc[tt], a, b0, b1);
-            }
-        }
-    }
-
     // publish this warp's partial tile
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            part[warp][g][8 * tt + 2 * t + e] = acc[tt][e];
-            part[warp][g + 8][8 * tt + 2 * t + e] = acc[tt][2 + e];
+            part[warp][g][8 * tt + 2 * t + e] += acc[tt][e];
+            part[warp][g + 8][8 * tt + 2 * t + e] += acc[tt][2 + e];
         }
     __syncwarp();
-
-    // outlier replacement over this rank's K range: lanes l and l+16 share
-    // tile row l % 16 and take alternate entries of its chunk-CSR range
-    if (p.off != nullptr && c_begin < c_end) {
-        const int kb = c_begin * kChunk;
-        const int ke = min(p.K, c_end * kChunk);
-        const int rl = lane & 15;
-        const int row = tile_row0 + rl;
-        float os[MT];
-#pragma unroll
-        for (int m = 0; m < MT; ++m) os[m] = 0.f;
-        if (PREPACKED && row < p.N) {
-            // global columns and ready corrections: two independent loads per
-            // entry, then the activations; four entries in flight per lane
-            const int32_t* ro = p.off + (int64_t)row * (p.ncsr + 1);
-            const int ia = __ldg(ro + kb / p.chunk_m), ib = __ldg(ro + (ke - 1) / p.chunk_m + 1);
-            const float* dl = reinterpret_cast<const float*>(p.cvals);
-            for (int i0 = ia + (lane >> 4); i0 < ib; i0 += 8) {
-                int col[4];
-                float d[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int i = i0 + 2 * u;
-                    col[u] = i < ib ? (int)(__ldg(reinterpret_cast<const uint32_t*>(p.ccols) + i) & 0xFFFFu) : -1;
-                    d[u] = i < ib ? __ldg(dl + i) : 0.f;
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    if (col[u] < kb || col[u] >= ke) continue;
-#pragma unroll
-                    for (int m = 0; m < MT; ++m)
-                        if (m < p.M) os[m] += d[u] * x_at(m, col[u]);
-                }
-            }
-        } else if (row < p.N) {
-            const int32_t* ro = p.off + (int64_t)row * (p.ncsr + 1);
-            int cc = kb / p.chunk_m;
-            const int cc_hi = (ke - 1) / p.chunk_m;
-            int bound = __ldg(ro + cc + 1);  // end of chunk cc
-            const int ib = __ldg(ro + cc_hi + 1);
-            for (int i = __ldg(ro + cc) + (lane >> 4); i < ib; i += 2) {
-                while (i >= bound) bound = __ldg(ro + (++cc) + 1);  // entries are chunk-ordered
-                const int col = cc * p.chunk_m + (int)__ldg(reinterpret_cast<const uint16_t*>(p.ccols) + i);
-                if (col < kb || col >= ke) continue;
-                const uint32_t sym = (__ldg(p.q + (int64_t)row * p.wpr + (col >> 3)) >> (4 * (col & 7))) & 15u;
-                const int grp = GROUPED ? ((col + p.goff) >> p.log2G) : 0;
-                const float wl = codebook_value<T, PREPACKED>(p.lut, (int64_t)row * p.ngroups + grp, sym);
-                const float d =
-                    f16_bits_to_f32(fp8_byte_to_f16_bits(__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i))) - wl;
-#pragma unroll
-                for (int m = 0; m < MT; ++m)
-                    if (m < p.M) os[m] += d * x_at(m, col);
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < MT; ++m) os[m] += __shfl_down_sync(0xFFFFFFFFu, os[m], 16);
-        if (lane < 16) {
-#pragma unroll
-            for (int m = 0; m < MT; ++m) part[warp][rl][m] += os[m];
-        }
-        __syncwarp();
-    }
 
     const bool clustered = gridDim.y > 1;
     if (clustered) cluster_sync_all();  // every rank's partial tiles are visible cluster-wide
