@@ -137,6 +137,39 @@ WLQ_API int wlq_dequant(const int32_t* q_packed, const void* lut_c, void* W_out,
  * the kernels of this library need no workspace, so this only validates. */
 WLQ_API int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device);
 
+/* ------------------------------------------------ tensor parallelism --- */
+/* Row-parallel layers (o, down) need the sum of every rank's partial output.
+ * wlq_gemv_allreduce fuses that all-reduce into the GEMV epilogue over NVLink
+ * peer memory: each rank pushes its gamma-scaled tile into every rank's
+ * communication buffer, publishes a per-tile epoch, waits (bounded, 2 s) for
+ * all ranks' epochs and sums.  Each rank allocates one buffer of
+ * wlq_tp_buffer_bytes(world, max_N) with wlq_tp_buffer_alloc, exchanges the
+ * 64-byte IPC handles with the other ranks (any host channel) and maps theirs
+ * with wlq_tp_buffer_open.  All ranks must issue the same sequence of calls.
+ * No reference counterpart: the reference leaves the all-reduce to vLLM's
+ * NCCL call after the layer (vllm: model_executor/layers/linear.py:1558-1559). */
+WLQ_API size_t wlq_tp_buffer_bytes(int world, int max_N);
+/* cudaMalloc'd and zeroed on the current device; handle_out receives the
+ * cudaIpcMemHandle_t (64 bytes).  Setup only: the one allocating entry point
+ * besides the codec helpers. */
+WLQ_API int wlq_tp_buffer_alloc(size_t bytes, void** ptr_out, unsigned char handle_out[64]);
+WLQ_API int wlq_tp_buffer_open(const unsigned char handle[64], void** ptr_out);
+WLQ_API int wlq_tp_buffer_close(void* peer_ptr);
+WLQ_API int wlq_tp_buffer_free(void* ptr);
+/* Reads (and optionally clears) the error word of this rank's buffer: bit 0
+ * set when a fused all-reduce gave up waiting for a rank (its output is then
+ * undefined).  Synchronous. */
+WLQ_API int wlq_tp_error(void* local_buf, unsigned int* flags_out, int clear);
+/* wlq_gemv (M <= 16) on this rank's K shard with the all-reduce of out over
+ * the tp_world ranks fused; tp_bufs[q] is rank q's buffer as mapped in this
+ * process (tp_bufs[tp_rank] the local one), max_N the N it was sized for. */
+WLQ_API int wlq_gemv_allreduce(const int32_t* q_packed, const void* lut_c, const void* x, void* out,
+             const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
+             const void* lora_B, const float* lora_h, const void* dora_gamma, float lora_scale,
+             int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
+             int lut_group_offset, int lut_format, int act_dtype, void* const* tp_bufs, int tp_rank,
+             int tp_world, int max_N, wlq_stream_t stream);
+
 /* Device error word of `device`: bit 0 (WLQ_DEVERR_WAIT_TIMEOUT) is set when
  * a pipeline wait inside a tensor-core GEMM kernel gave up (the kernel then
  * abandons its tile and its output is undefined).  Synchronous; clears the

@@ -167,6 +167,26 @@ def gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offse
     check(rc, "wlq_gemm")
 
 
+def gemv_allreduce(comm, X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,
+                   chunk_vals=None, lora_H=None, lora_B=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
+                   lut_group_offset=0, lut_format=WLQ_LUT_F16):
+    """Row-parallel decode forward (M <= 16) on this rank's K shard with the
+    all-reduce of `out` over `comm`'s ranks fused into the kernel (see
+    qwen_wlqfastshot_helen_beta_b200.tp.TPComm).  Every rank of the group
+    must make the same calls in the same order."""
+    N, K, bits, wpr = int(N), int(K), int(bits), int(words_per_row)
+    offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
+    lb, lh, gm = _opt(lora_B), _opt(lora_H), _opt(dora_gamma)
+    M, r = _linear_checks("gemv_allreduce", X, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lb, lh, gm,
+                          int(lut_group_size), int(lut_group_offset), int(lut_format))
+    with _DeviceGuard(X.device):
+        rc = lib.wlq_gemv_allreduce(_ptr(q_packed), _ptr(lut_c), _ptr(X), _ptr(out), _ptr(offs), _ptr(cols),
+                                    _ptr(vals), _ptr(lb), _ptr(lh), _ptr(gm), float(lora_scale), r, M, N, K, bits,
+                                    wpr, int(lut_group_size), int(lut_group_offset), int(lut_format), _act_dtype(X),
+                                    comm.bufs, comm.rank, comm.world, comm.max_N, _stream(X.device))
+    check(rc, "wlq_gemv_allreduce")
+
+
 def dequant_w0(q_packed, lut_c, W_out, N, K, bits, words_per_row, chunk_offsets, chunk_cols, chunk_vals,
                lut_group_size=0, lut_group_offset=0):
     """Dense fp16 W = codebook[q] with outliers replaced, bit-exact

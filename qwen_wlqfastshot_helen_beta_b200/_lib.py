@@ -36,6 +36,14 @@ SIGNATURES = {
     "wlq_dequant": (_i32, [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p]),
     "wlq_init_workspaces": (_i32, [_i64, _i64, _i32]),
     "wlq_device_error": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint), _i32]),
+    "wlq_tp_buffer_bytes": (ctypes.c_size_t, [_i32, _i32]),
+    "wlq_tp_buffer_alloc": (_i32, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
+    "wlq_tp_buffer_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "wlq_tp_buffer_close": (_i32, [_p]),
+    "wlq_tp_buffer_free": (_i32, [_p]),
+    "wlq_tp_error": (_i32, [_p, ctypes.POINTER(ctypes.c_uint), _i32]),
+    "wlq_gemv_allreduce": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
+                                  _i32, _i32, _i32, _i32, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i32, _p]),
     "wlq_words_per_row": (_i64, [_i64, _i32]),
     "wlq_repack_q_indices_row_aligned": (_i32, [_p, _i64, _i64, _i64, _i32, _p, _i64, _p64]),
     "wlq_repack_q_indices_slice": (_i32, [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i64, _p, _i64, _p64]),

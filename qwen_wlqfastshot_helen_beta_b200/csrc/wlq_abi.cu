@@ -239,6 +239,91 @@ int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device) {
     return WLQ_OK;
 }
 
+size_t wlq_tp_buffer_bytes(int world, int max_N) {
+    if (world < 1 || world > 8 || max_N < 0) return 0;
+    return tp_layout(world, max_N).total;
+}
+
+int wlq_tp_buffer_alloc(size_t bytes, void** ptr_out, unsigned char handle_out[64]) {
+    g_last_error[0] = '\0';
+    if (!ptr_out || !handle_out || bytes == 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_tp_buffer_alloc: bad arguments");
+    int rc = require_sm100();
+    if (rc) return rc;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return check_cuda(e, "wlq_tp_buffer_alloc: cudaMalloc");
+    if ((e = cudaMemset(p, 0, bytes)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+        cudaFree(p);
+        return check_cuda(e, "wlq_tp_buffer_alloc: clear");
+    }
+    cudaIpcMemHandle_t h;
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    if ((e = cudaIpcGetMemHandle(&h, p)) != cudaSuccess) {
+        cudaFree(p);
+        return check_cuda(e, "wlq_tp_buffer_alloc: cudaIpcGetMemHandle");
+    }
+    memcpy(handle_out, &h, 64);
+    *ptr_out = p;
+    return WLQ_OK;
+}
+
+int wlq_tp_buffer_open(const unsigned char handle[64], void** ptr_out) {
+    g_last_error[0] = '\0';
+    if (!handle || !ptr_out) return fail(WLQ_ERR_INVALID_ARG, "wlq_tp_buffer_open: bad arguments");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, 64);
+    return check_cuda(cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess), "wlq_tp_buffer_open");
+}
+
+int wlq_tp_buffer_close(void* peer_ptr) {
+    g_last_error[0] = '\0';
+    return check_cuda(cudaIpcCloseMemHandle(peer_ptr), "wlq_tp_buffer_close");
+}
+
+int wlq_tp_buffer_free(void* ptr) {
+    g_last_error[0] = '\0';
+    return check_cuda(cudaFree(ptr), "wlq_tp_buffer_free");
+}
+
+int wlq_tp_error(void* local_buf, unsigned int* flags_out, int clear) {
+    g_last_error[0] = '\0';
+    if (!local_buf || !flags_out) return fail(WLQ_ERR_INVALID_ARG, "wlq_tp_error: bad arguments");
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpy(&v, local_buf, sizeof(v), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(local_buf, 0, sizeof(v));
+    if (e != cudaSuccess) return check_cuda(e, "wlq_tp_error");
+    *flags_out = v;
+    return WLQ_OK;
+}
+
+int wlq_gemv_allreduce(const int32_t* q_packed, const void* lut_c, const void* x, void* out,
+                       const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
+                       const void* lora_B, const float* lora_h, const void* dora_gamma, float lora_scale, int r,
+                       int M, int N, int K, int bits, int words_per_row, int lut_group_size, int lut_group_offset,
+                       int lut_format, int act_dtype, void* const* tp_bufs, int tp_rank, int tp_world, int max_N,
+                       wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    LinearArgs a;
+    int rc = build_args("wlq_gemv_allreduce", x, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B,
+                        lora_h, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size,
+                        lut_group_offset, lut_format, act_dtype, a);
+    if (rc) return rc;
+    if (M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_allreduce: M must be 1..16 (got %d)", M);
+    if (tp_world < 2 || tp_world > 8 || tp_rank < 0 || tp_rank >= tp_world || !tp_bufs)
+        return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_allreduce: bad rank %d of %d", tp_rank, tp_world);
+    if (N > max_N) return fail(WLQ_ERR_CAPACITY, "wlq_gemv_allreduce: N=%d exceeds the buffers' max_N=%d", N, max_N);
+    for (int q = 0; q < tp_world; ++q)
+        if (!tp_bufs[q] || !aligned(tp_bufs[q], 256))
+            return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_allreduce: buffer of rank %d missing or misaligned", q);
+    if (M == 0 || N == 0) return WLQ_OK;
+    if ((rc = require_sm100())) return rc;
+    a.tp_world = tp_world;
+    a.tp_rank = tp_rank;
+    a.tp_nmax = max_N;
+    for (int q = 0; q < tp_world; ++q) a.tp_bufs[q] = tp_bufs[q];
+    return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int wlq_device_error(int device, unsigned int* flags_out, int clear) {
     g_last_error[0] = '\0';
     if (!flags_out || device < 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_device_error: bad arguments");

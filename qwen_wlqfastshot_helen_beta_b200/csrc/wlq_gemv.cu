@@ -43,6 +43,7 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kRowsPerTile = 16;
 constexpr int kChunk = 128;  // k columns per warp iteration
+constexpr int kMaxTp = 8;    // ranks of a fused all-reduce
 
 struct GemvParams {
     const uint32_t* q;
@@ -63,6 +64,12 @@ struct GemvParams {
     int x_stride;          // shared-memory row stride of staged activations (elements)
     int x_bytes;           // bytes of dynamic shared memory before the ring (staged activations)
     uint32_t mul16, mul31; // 1<<16 and 1<<31, runtime values so mul.hi stays a multiply
+    // fused tensor-parallel all-reduce (row-parallel layers), tp_world > 1
+    int tp_world, tp_rank, tp_nmax;
+    float* tp_data[kMaxTp];      // each rank's slots [2 parities][world][16 tokens][tp_nmax] fp32
+    uint32_t* tp_flags[kMaxTp];  // each rank's per-tile epochs [tiles][world]
+    uint32_t* tp_counters;       // this rank's per-tile call counters [tiles]
+    uint32_t* tp_err;            // this rank's error word
 };
 
 // Codebook value of symbol q of one (row, group) as the MMA saw it.
@@ -110,6 +117,79 @@ struct Ring {
     static constexpr int kPlaneBytes = kRowsPerTile * NSLOT * 32;
     static constexpr int kStageBytes = kIdxBytes + kPlaneBytes;
 };
+
+__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// Row-parallel epilogue with the all-reduce fused, for one warp's 16-row
+// tile (cluster rank 0): the tile's gamma-scaled partial results are pushed
+// into slot [parity][this rank] of every rank's buffer over NVLink peer
+// stores, the tile's epoch is published to every rank with a system-scope
+// release store, and once every rank's epoch for the tile has arrived
+// (bounded wait) the local slots are summed into out.  Epochs come from a
+// per-tile call counter that advances identically on every rank, so CUDA
+// graph replays need no host input; slots alternate by epoch parity, and a
+// rank cannot run two calls ahead on a tile because each call waits for all
+// ranks' data of the previous one.
+template <typename T, int MT>
+__device__ void tp_allreduce_tile(const GemvParams& p, float (*part)[MT], uint32_t nranks, int tile_row0, int lane) {
+    const int tile = tile_row0 / kRowsPerTile;
+    const int world = p.tp_world, me = p.tp_rank;
+    const bool clustered = nranks > 1;
+    uint32_t cnt = lane == 0 ? p.tp_counters[tile] + 1u : 0u;
+    cnt = __shfl_sync(0xFFFFFFFFu, cnt, 0);
+    const int par = (int)(cnt & 1u);
+    const bool dora = p.r > 0;
+    for (int e = lane; e < kRowsPerTile * MT; e += 32) {
+        const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
+        const int n = tile_row0 + rl;
+        if (n >= p.N || tk >= p.M) continue;
+        float s = part[rl][tk];
+        if (clustered) {
+            const uint32_t a = smem_u32(&part[rl][tk]);
+            for (uint32_t qq = 1; qq < nranks; ++qq) s += ld_shared_cluster_f32(mapa_shared(a, qq));
+        }
+        if (dora) s *= f16_bits_to_f32(__ldg(p.gamma + n));
+        const int64_t slot = ((int64_t)(par * world + me) * kRowsPerTile + tk) * p.tp_nmax + n;
+        for (int q = 0; q < world; ++q) p.tp_data[q][slot] = s;
+    }
+    __threadfence_system();  // this lane's peer stores before the epoch
+    __syncwarp();
+    int ok = 1;
+    if (lane == 0) {
+        for (int q = 0; q < world; ++q) st_release_sys(p.tp_flags[q] + tile * world + me, cnt);
+        const uint32_t* mine = p.tp_flags[me] + tile * world;
+        const uint64_t t0 = globaltimer_ns();
+        for (int q = 0; q < world && ok; ++q) {
+            while (ld_acquire_sys(mine + q) < cnt) {
+                if (globaltimer_ns() - t0 > 2000000000ull) {  // a rank never arrived: give up
+                    atomicOr(p.tp_err, 1u);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        p.tp_counters[tile] = cnt;
+    }
+    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+    __threadfence();
+    if (!ok) return;
+    for (int e = lane; e < kRowsPerTile * MT; e += 32) {
+        const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
+        const int n = tile_row0 + rl;
+        if (n >= p.N || tk >= p.M) continue;
+        float s = 0.f;
+        for (int q = 0; q < world; ++q)
+            s += __ldcg(p.tp_data[me] + ((int64_t)(par * world + q) * kRowsPerTile + tk) * p.tp_nmax + n);
+        reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s);
+    }
+}
 
 template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int S>
 __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p) {
@@ -402,7 +482,9 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
     const bool clustered = gridDim.y > 1;
     if (clustered) cluster_sync_all();  // every rank's partial tiles are visible cluster-wide
     const uint32_t rank = clustered ? cluster_ctarank() : 0u;
-    if (rank == 0) {
+    if (rank == 0 && p.tp_world > 1) {
+        tp_allreduce_tile<T, MT>(p, part[warp], clustered ? cluster_nctarank() : 1u, tile_row0, lane);
+    } else if (rank == 0) {
         const uint32_t nranks = clustered ? cluster_nctarank() : 1u;
         const bool dora = p.r > 0;
         for (int e = lane; e < kRowsPerTile * MT; e += 32) {
@@ -506,6 +588,20 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     p.kchunks = (a.K + kChunk - 1) / kChunk;
     p.mul16 = 1u << 16;
     p.mul31 = 1u << 31;
+    p.tp_world = a.tp_world;
+    p.tp_rank = a.tp_rank;
+    p.tp_nmax = a.tp_nmax;
+    if (a.tp_world > 1) {
+        const TpLayout l = tp_layout(a.tp_world, a.tp_nmax);
+        for (int q = 0; q < a.tp_world; ++q) {
+            char* b = static_cast<char*>(a.tp_bufs[q]);
+            p.tp_data[q] = reinterpret_cast<float*>(b + l.data);
+            p.tp_flags[q] = reinterpret_cast<uint32_t*>(b + l.flags);
+        }
+        char* mine = static_cast<char*>(a.tp_bufs[a.tp_rank]);
+        p.tp_counters = reinterpret_cast<uint32_t*>(mine + l.counters);
+        p.tp_err = reinterpret_cast<uint32_t*>(mine + l.err);
+    }
     const bool xvec = (a.K % 8 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
 
     const int tiles = (a.N + kRowsPerTile - 1) / kRowsPerTile;

@@ -36,7 +36,28 @@ struct LinearArgs {
     int ncsr;                // outlier chunks per row
     int dtype;               // WLQ_DTYPE_*
     bool lut_prepacked;      // WLQ_LUT_PREPACKED codebooks
+    // fused tensor-parallel all-reduce (wlq_gemv_allreduce); tp_world = 1: off
+    int tp_world = 1, tp_rank = 0, tp_nmax = 0;
+    void* tp_bufs[8] = {};   // every rank's communication buffer (this process's mappings)
 };
+
+// Layout of a tensor-parallel communication buffer (one per rank, shared
+// through CUDA IPC): error word, per-tile call counters (local use), per-tile
+// epochs written by every rank, then [2][world][16][max_N] fp32 slots.
+struct TpLayout {
+    size_t err, counters, flags, data, total;
+};
+inline TpLayout tp_layout(int world, int max_N) {
+    auto up = [](size_t v, size_t a) { return (v + a - 1) / a * a; };
+    const size_t tiles = (size_t)(max_N + 15) / 16;
+    TpLayout l;
+    l.err = 0;
+    l.counters = 128;
+    l.flags = up(l.counters + 4 * tiles, 128);
+    l.data = up(l.flags + 4 * tiles * (size_t)world, 256);
+    l.total = up(l.data + 2ull * world * 16 * (size_t)max_N * 4, 256);
+    return l;
+}
 
 int launch_gemv(const LinearArgs& a, cudaStream_t stream);
 int launch_gemm(const LinearArgs& a, cudaStream_t stream);

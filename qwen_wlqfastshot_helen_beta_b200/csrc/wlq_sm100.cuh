@@ -18,11 +18,6 @@ static __device__ unsigned int g_wlq_device_error = 0;
 constexpr unsigned int kErrWaitTimeout = 1u;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

@@ -1,0 +1,115 @@
+"""Fused row-parallel all-reduce (wlq_gemv_allreduce) on 2 GPUs: each rank's
+K shard through the GEMV with the sum over ranks done in the kernel over
+NVLink peer memory, against the ranks' own outputs summed after an NCCL
+all-gather.  Eager calls and CUDA-graph replays (the per-tile epochs advance
+on the device), several token counts.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, port, results):
+    import sys
+    sys.path.insert(0, ROOT)
+    from datetime import timedelta
+    import torch.distributed as dist
+    from qwen_wlqfastshot_helen_beta_b200 import _C, synthetic as S
+    from qwen_wlqfastshot_helen_beta_b200.tp import TPComm
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    comm = None
+    try:
+        N, Kp = 3584, 1792  # row-parallel shard of a 3584-wide K
+        L = S.make_layer(N, Kp, group_size=128, density=0.005, r=16, seed=40 + rank, device=dev)
+        L.prepack(torch.bfloat16)
+        comm = TPComm(max_N=N)
+        lut, cols, vals, fmt = L.operands_for(torch.bfloat16)
+        errs = []
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(9 + rank)
+
+        def fused(x, h, out):
+            _C.gemv_allreduce(comm, x, L.q_packed, lut, out, N, Kp, 4, L.words_per_row, L.chunk_offsets, cols,
+                              vals, h, L.lora_B, L.dora_gamma, L.lora_scale, L.group_size, L.group_offset, fmt)
+
+        def check(x, h, y):
+            own = S.forward(L, x, h=h).float()
+            parts = [torch.empty_like(own) for _ in range(2)]
+            dist.all_gather(parts, own)
+            ref = parts[0] + parts[1]
+            errs.append(float((y.float() - ref).abs().max() / ref.abs().max()))
+
+        for M in (1, 5, 16):
+            for _ in range(3):  # repeated calls: epochs and slot parity advance
+                x = torch.randn((M, Kp), generator=gen, device=dev).to(torch.bfloat16)
+                h = S.lora_h(L, x)
+                y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+                fused(x, h, y)
+                check(x, h, y)
+        # the same inside a CUDA graph, replayed with new inputs
+        M = 8
+        x = torch.randn((M, Kp), generator=gen, device=dev).to(torch.bfloat16)
+        h = S.lora_h(L, x)
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        fused(x, h, y)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                fused(x, h, y)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            x.copy_(torch.randn((M, Kp), generator=gen, device=dev).to(torch.bfloat16))
+            h.copy_(S.lora_h(L, x))
+            dist.barrier()
+            g.replay()
+            torch.cuda.synchronize()
+            check(x, h, y)
+        del g
+        torch.cuda.synchronize()
+        results[rank] = {"errs": errs, "flag": comm.error()}
+    finally:
+        dist.barrier()
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_fused_allreduce_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for r in range(2):
+        res = dict(results[r])
+        assert res["flag"] == 0, res
+        assert max(res["errs"]) <= 1e-2, res
