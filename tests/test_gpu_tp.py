@@ -113,3 +113,46 @@ def test_fused_allreduce_two_gpus():
         res = dict(results[r])
         assert res["flag"] == 0, res
         assert max(res["errs"]) <= 1e-2, res
+
+
+def test_fused_allreduce_wait_runs_out():
+    """A peer that never arrives: rank 0 of a 2-rank group whose second
+    buffer nobody writes.  The kernel's bounded wait gives up (2 s), sets the
+    error word and returns; the context stays usable."""
+    import ctypes
+    import time
+    from qwen_wlqfastshot_helen_beta_b200 import _C, _lib, synthetic as S
+    lib = _lib.lib
+    N, K = 64, 512
+    bufs = []
+    for _ in range(2):
+        ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        _lib.check(lib.wlq_tp_buffer_alloc(int(lib.wlq_tp_buffer_bytes(2, N)), ctypes.byref(ptr), handle), "alloc")
+        bufs.append(ptr.value)
+
+    class Lonely:  # the shape TPComm has, with a silent second rank
+        world, rank, max_N = 2, 0, N
+        bufs_c = (ctypes.c_void_p * 2)(*bufs)
+    Lonely.bufs = Lonely.bufs_c
+    try:
+        L = S.make_layer(N, K, group_size=128, density=0.01, r=16, seed=3).prepack(torch.bfloat16)
+        x = torch.randn((2, K), device="cuda").to(torch.bfloat16)
+        h = S.lora_h(L, x)
+        y = torch.zeros((2, N), dtype=torch.bfloat16, device="cuda")
+        t0 = time.time()
+        _C.gemv_allreduce(Lonely, x, L.q_packed, L.lut_packed, y, N, K, 4, L.words_per_row, L.chunk_offsets,
+                          L.cols_packed, L.delta_packed, h, L.lora_B, L.dora_gamma, L.lora_scale, L.group_size,
+                          L.group_offset, 1)
+        torch.cuda.synchronize()
+        waited = time.time() - t0
+        flags = ctypes.c_uint(0)
+        _lib.check(lib.wlq_tp_error(ctypes.c_void_p(bufs[0]), ctypes.byref(flags), 1), "wlq_tp_error")
+        assert flags.value & 1, "the wait should have run out"
+        assert 1.0 < waited < 30.0, waited
+        # the context is still usable: a plain call gives the right answer
+        ref = S.forward(L, x, h=h)
+        again = S.forward(L, x, h=h)
+        assert torch.equal(ref, again)
+    finally:
+        for b in bufs:
+            lib.wlq_tp_buffer_free(ctypes.c_void_p(b))
