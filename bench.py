@@ -340,35 +340,40 @@ def run_ours(args):
 
     # ---- e2e: public op, host activations in, outputs out, every step
     import qwen_wlqfastshot_helen_beta_b200  # noqa: F401  (torch ops)
-    host = []
-    for (c, name, M, L, x, h, out) in per_copy[0]:
-        xh = x.cpu().pin_memory()
-        hh = h.cpu().pin_memory()
-        oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        host.append((name, M, L, xh, hh, oh, torch.empty_like(x), torch.empty_like(h), torch.empty_like(out)))
-    h2d = sum(xh.numel() * xh.element_size() + hh.numel() * hh.element_size() for (_, _, _, xh, hh, *_r) in host)
-    d2h = sum(oh.numel() * oh.element_size() for (_, _, _, _, _, oh, *_r) in host)
+    # a step's activations (x and h of every launch) sit in one pinned host
+    # buffer and go over in one copy; the outputs land in one device buffer
+    # and come back in one copy, the way a serving stack stages a batch
+    def arena(tensors):
+        offs, n = [], 0
+        for t in tensors:
+            offs.append(n)
+            n += (t.numel() * t.element_size() + 255) // 256 * 256
+        return offs, n
 
-    def e2e_step():
-        for (name, M, L, xh, hh, oh, xd, hd, od) in host:
-            xd.copy_(xh, non_blocking=True)
-            hd.copy_(hh, non_blocking=True)
-            if comm is not None and name in ("o", "down"):
-                _C.gemv_allreduce(comm, xd, L.q_packed, L.lut_packed, od, L.N, L.K, 4, L.words_per_row,
-                                  L.chunk_offsets, L.cols_packed, L.delta_packed, hd, L.lora_B, L.dora_gamma,
-                                  L.lora_scale, L.group_size, L.group_offset, 1)
-            else:
-                torch.ops.wlq_fastShot.gemm(xd, L.q_packed, L.lut_packed, od, L.N, L.K, 4, L.words_per_row,
-                                            L.chunk_offsets, L.cols_packed, L.delta_packed, hd, L.lora_B,
-                                            L.dora_gamma, L.lora_scale, L.group_size, L.group_offset, 1)
-            reduce_if_rowpar(name, od)
-            oh.copy_(od, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+    ins = [t for (_, _, _, _, x, h, _) in per_copy[0] for t in (x, h)]
+    outs = [out for (*_r, out) in per_copy[0]]
+    in_offs, in_n = arena(ins)
+    out_offs, out_n = arena(outs)
+    in_host = torch.empty(in_n, dtype=torch.uint8).pin_memory()
+    in_dev = torch.empty(in_n, dtype=torch.uint8, device=dev)
+    out_host = torch.empty(out_n, dtype=torch.uint8).pin_memory()
+    out_dev = torch.empty(out_n, dtype=torch.uint8, device=dev)
+
+    def view(buf, off, t):
+        return buf[off:off + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
+
+    for t, o in zip(ins, in_offs):
+        view(in_host, o, t).copy_(t.cpu())
+    host = []
+    for i, (c, name, M, L, x, h, out) in enumerate(per_copy[0]):
+        host.append((name, L, view(in_dev, in_offs[2 * i], x), view(in_dev, in_offs[2 * i + 1], h),
+                     view(out_dev, out_offs[i], out)))
+    h2d = sum(t.numel() * t.element_size() for t in ins)
+    d2h = sum(t.numel() * t.element_size() for t in outs)
 
     def e2e_enqueue():
-        for (name, M, L, xh, hh, oh, xd, hd, od) in host:
-            xd.copy_(xh, non_blocking=True)
-            hd.copy_(hh, non_blocking=True)
+        in_dev.copy_(in_host, non_blocking=True)
+        for (name, L, xd, hd, od) in host:
             if comm is not None and name in ("o", "down"):
                 _C.gemv_allreduce(comm, xd, L.q_packed, L.lut_packed, od, L.N, L.K, 4, L.words_per_row,
                                   L.chunk_offsets, L.cols_packed, L.delta_packed, hd, L.lora_B, L.dora_gamma,
@@ -378,7 +383,11 @@ def run_ours(args):
                                             L.chunk_offsets, L.cols_packed, L.delta_packed, hd, L.lora_B,
                                             L.dora_gamma, L.lora_scale, L.group_size, L.group_offset, 1)
             reduce_if_rowpar(name, od)
-            oh.copy_(od, non_blocking=True)
+        out_host.copy_(out_dev, non_blocking=True)
+
+    def e2e_step():
+        e2e_enqueue()
+        torch.cuda.current_stream().synchronize()
 
     def timed_e2e(step_fn):
         for _ in range(args.warmup):
@@ -454,9 +463,9 @@ def run_ours(args):
             },
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "path": "torch.ops.wlq_fastShot.gemm on every (linear, M) of a step, inputs copied from pinned "
-                            "host memory and outputs read back every step; the step replayed as one CUDA graph "
-                            "(as vLLM runs decode), host synchronised per step",
+                    "path": "torch.ops.wlq_fastShot.gemm on every (linear, M) of a step; the step's activations "
+                            "copied from one pinned host buffer and its outputs read back into one, every step; "
+                            "the step replayed as one CUDA graph (as vLLM runs decode), host synchronised per step",
                     "eager_value": round(eager_value, 1)},
             "gpu_launches": 16 * args.steps,
             "clocks": clk.summary(),
