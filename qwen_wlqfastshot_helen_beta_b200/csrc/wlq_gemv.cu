@@ -83,12 +83,13 @@ __device__ __forceinline__ float codebook_value(const uint16_t* __restrict__ lut
     return ActTraits<T>::bits_to_f32(ActTraits<T>::from_f16_bits(__ldg(lut + entry * 16 + q)));
 }
 
-// Stages x[0:M, kb:kb+cols) into shared memory, rows padded by 8 elements
-// (16 bytes) so the per-token rows fall in different banks; columns past K
-// read as zero.  16-byte cp.async when rows of x are 16-byte aligned.
+// Issues the staging of x[0:M, kb:kb+cols) into shared memory as one
+// cp.async group (the caller waits for it), rows padded by 8 elements (16
+// bytes) so the per-token rows fall in different banks; columns past K read
+// as zero.  16-byte cp.async when rows of x are 16-byte aligned.
 template <typename T, bool XVEC>
-__device__ __forceinline__ void stage_x(uint16_t* xs, const T* __restrict__ x, int M, int K, int kb, int cols,
-                                        int stride) {
+__device__ __forceinline__ void stage_x_issue(uint16_t* xs, const T* __restrict__ x, int M, int K, int kb, int cols,
+                                              int stride) {
     const uint16_t* xg = reinterpret_cast<const uint16_t*>(x);
     const int pieces = cols / 8;
     for (int e = threadIdx.x; e < M * pieces; e += blockDim.x) {
@@ -103,7 +104,21 @@ __device__ __forceinline__ void stage_x(uint16_t* xs, const T* __restrict__ x, i
             for (int j = 0; j < 8; ++j) dst[j] = k + j < K ? xg[(int64_t)m * K + k + j] : (uint16_t)0;
         }
     }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    cp_async_commit();
+}
+
+// Sum over the cluster's ranks of one partial-tile element, rank 0 first:
+// the remote loads are all issued before the adds.
+__device__ __forceinline__ float cluster_sum(const float* own, uint32_t nranks) {
+    if (nranks == 1) return *own;
+    const uint32_t a = smem_u32(own);
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = (uint32_t)q < nranks ? ld_shared_cluster_f32(mapa_shared(a, (uint32_t)q)) : 0.f;
+    float s = v[0];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) s += v[q];
+    return s;
 }
 
 // Per-warp shared-memory ring of S stages, filled by cp.async (no register
@@ -138,24 +153,19 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
 // rank cannot run two calls ahead on a tile because each call waits for all
 // ranks' data of the previous one.
 template <typename T, int MT>
-__device__ void tp_allreduce_tile(const GemvParams& p, float (*part)[MT], uint32_t nranks, int tile_row0, int lane) {
+__device__ void tp_allreduce_tile(const GemvParams& p, float (*part)[MT], uint32_t nranks, int tile_row0, int lane,
+                                  float gam) {
     const int tile = tile_row0 / kRowsPerTile;
     const int world = p.tp_world, me = p.tp_rank;
     const bool clustered = nranks > 1;
     uint32_t cnt = lane == 0 ? p.tp_counters[tile] + 1u : 0u;
     cnt = __shfl_sync(0xFFFFFFFFu, cnt, 0);
     const int par = (int)(cnt & 1u);
-    const bool dora = p.r > 0;
     for (int e = lane; e < kRowsPerTile * MT; e += 32) {
         const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
         const int n = tile_row0 + rl;
         if (n >= p.N || tk >= p.M) continue;
-        float s = part[rl][tk];
-        if (clustered) {
-            const uint32_t a = smem_u32(&part[rl][tk]);
-            for (uint32_t qq = 1; qq < nranks; ++qq) s += ld_shared_cluster_f32(mapa_shared(a, qq));
-        }
-        if (dora) s *= f16_bits_to_f32(__ldg(p.gamma + n));
+        const float s = cluster_sum(&part[rl][tk], clustered ? nranks : 1u) * gam;
         const int64_t slot = ((int64_t)(par * world + me) * kRowsPerTile + tk) * p.tp_nmax + n;
         for (int q = 0; q < world; ++q) p.tp_data[q][slot] = s;
     }
@@ -251,6 +261,10 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
     };
 #pragma unroll
     for (int j = 0; j < S - 1; ++j) issue(c_begin + j, j);
+    // this rank's activations into shared memory (XSMEM), waited for after
+    // the low-rank MMA; larger slices are read through L1
+    const int kb0 = c_begin * kChunk;
+    if (XSMEM) stage_x_issue<T, XVEC>(xs, x, p.M, p.K, kb0, p.chunks_per_rank * kChunk, p.x_stride);
 
     // per-row codebooks (no grouping) stay in registers for the whole K range
     LutPlanes PR0, PR1;
@@ -274,6 +288,9 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
         o_ia = __ldg(ro + c_begin * kChunk / p.chunk_m);
         o_ib = __ldg(ro + (min(p.K, c_end * kChunk) - 1) / p.chunk_m + 1);
     }
+    // DoRA magnitude of the row this lane finishes in the epilogue
+    const int erow = tile_row0 + (lane & 15);
+    const float gam = (p.r > 0 && erow < p.N) ? f16_bits_to_f32(__ldg(p.gamma + erow)) : 1.f;
 
     // DoRA low-rank term s * B h on the tensor core, once per output tile
     // (cluster rank 0), into the accumulators before the main loop: A = the
@@ -308,11 +325,24 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
         }
     }
 
-    // this rank's activations into shared memory (XSMEM), or read through L1
-    // when the slice is too large to stage
-    const int kb0 = c_begin * kChunk;
+    // this lane's first outlier entries (prepacked layout: global columns
+    // and ready corrections), loaded before the activation wait; lanes l and
+    // l+16 take alternate entries of row l % 16, four in flight per lane
+    const uint32_t* orec = reinterpret_cast<const uint32_t*>(p.ccols);
+    const float* odel = reinterpret_cast<const float*>(p.cvals);
+    int ocol[4];
+    float odl[4];
+    auto load_outliers = [&](int i0, int ib) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = i0 + 2 * u;
+            ocol[u] = i < ib ? (int)(__ldg(orec + i) & 0xFFFFu) : -1;
+            odl[u] = i < ib ? __ldg(odel + i) : 0.f;
+        }
+    };
+    if (PREPACKED && o_has) load_outliers(o_ia + (lane >> 4), o_ib);
     if (XSMEM) {
-        stage_x<T, XVEC>(xs, x, p.M, p.K, kb0, p.chunks_per_rank * kChunk, p.x_stride);
+        cp_async_wait<0>();  // the staged activations (and the ring's first chunks)
         __syncthreads();
     }
     bool tok_ok[NT];
@@ -361,19 +391,18 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 #pragma unroll
         for (int m = 0; m < MT; ++m) os[m] = 0.f;
         if (PREPACKED && o_has) {
-            // global columns and ready corrections: two independent loads per
-            // entry, then the activations; four entries in flight per lane
-            const int ia = o_ia, ib = o_ib;
-            const float* dl = reinterpret_cast<const float*>(p.cvals);
-            for (int i0 = ia + (lane >> 4); i0 < ib; i0 += 8) {
+            // each batch of four entries is in registers before its
+            // activations are read; the next batch loads meanwhile
+            const int ib = o_ib;
+            for (int i0 = o_ia + (lane >> 4); i0 < ib; i0 += 8) {
                 int col[4];
                 float d[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const int i = i0 + 2 * u;
-                    col[u] = i < ib ? (int)(__ldg(reinterpret_cast<const uint32_t*>(p.ccols) + i) & 0xFFFFu) : -1;
-                    d[u] = i < ib ? __ldg(dl + i) : 0.f;
+                    col[u] = ocol[u];
+                    d[u] = odl[u];
                 }
+                if (i0 + 8 < ib) load_outliers(i0 + 8, ib);
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     if (col[u] < kb || col[u] >= ke) continue;
@@ -482,25 +511,22 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
     const bool clustered = gridDim.y > 1;
     if (clustered) cluster_sync_all();  // every rank's partial tiles are visible cluster-wide
     const uint32_t rank = clustered ? cluster_ctarank() : 0u;
-    if (rank == 0 && p.tp_world > 1) {
-        tp_allreduce_tile<T, MT>(p, part[warp], clustered ? cluster_nctarank() : 1u, tile_row0, lane);
-    } else if (rank == 0) {
-        const uint32_t nranks = clustered ? cluster_nctarank() : 1u;
-        const bool dora = p.r > 0;
+    const uint32_t nranks = clustered ? cluster_nctarank() : 1u;
+    if (p.tp_world > 1) {
+        if (rank == 0) tp_allreduce_tile<T, MT>(p, part[warp], nranks, tile_row0, lane, gam);
+    } else {
+        // every rank finishes the tile rows rl with rl % nranks == rank; the
+        // sum over ranks is in rank order, so the result does not depend on
+        // which rank computes it.  s * B h is already in the tile.
         for (int e = lane; e < kRowsPerTile * MT; e += 32) {
-            const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;  // rows fastest: coalesced stores
+            const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;  // rl == lane % 16
             const int n = tile_row0 + rl;
-            if (n >= p.N || tk >= p.M) continue;
-            float s = part[warp][rl][tk];
-            if (clustered) {
-                const uint32_t a = smem_u32(&part[warp][rl][tk]);
-                for (uint32_t qq = 1; qq < nranks; ++qq) s += ld_shared_cluster_f32(mapa_shared(a, qq));
-            }
-            if (dora) s *= f16_bits_to_f32(__ldg(p.gamma + n));  // s * B h is already in s
+            if (n >= p.N || tk >= p.M || (uint32_t)rl % nranks != rank) continue;
+            const float s = cluster_sum(&part[warp][rl][tk], nranks) * gam;
             reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s);
         }
     }
-    if (clustered) cluster_sync_all();  // keep every rank's tiles alive until rank 0 is done
+    if (clustered) cluster_sync_all();  // keep every rank's tiles alive until all reads are done
 }
 
 constexpr int kStages = 3;  // measured: 3 >= 4 > 6 (more stages cost occupancy, not latency)
