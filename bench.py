@@ -195,7 +195,7 @@ def full_layer_bytes(M):
         nnz = int(round(N * K * DENSITY))
         ncsr = (K + 511) // 512
         tot += N * wpr * 4 + N * ng * 32 + N * (ncsr + 1) * 4 + 3 * nnz
-        tot += N * RANK * 2 + N * 2 + M * RANK * 4 + M * K * 2 + M * N * 2
+        tot += N * RANK * 2 + N * 2 + RANK * K * 2 + M * K * 2 + M * N * 2
     return tot
 
 
@@ -219,16 +219,15 @@ def run_ours(args):
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
 
-    # resident inputs per (copy, linear, M)
-    calls = []  # (copy, name, M, layer, x, h, out)
+    # resident inputs per (copy, linear, M); the GEMV computes h = A x itself
+    calls = []  # (copy, name, M, layer, x, A, out)
     for c in range(copies):
         for name, K, N in SHAPES:
             L = layers[c][name]
             for M in MS:
                 x = torch.randn((M, L.K), generator=gen, device=dev).to(torch.bfloat16)
-                h = S.lora_h(L, x)
                 out = torch.empty((M, L.N), dtype=torch.bfloat16, device=dev)
-                calls.append((c, name, M, L, x, h, out))
+                calls.append((c, name, M, L, x, L.lora_A_act, out))
     lib = _lib.lib
     stream = torch.cuda.current_stream()
 
@@ -239,12 +238,25 @@ def run_ours(args):
         from qwen_wlqfastshot_helen_beta_b200.tp import TPComm
         comm = TPComm(max_N=max(N for _, _, N in SHAPES))
 
-    def launch(L, x, h, out, name=None):
+    def vp(t):
+        return ctypes.c_void_p(t.data_ptr())
+
+    def launch(L, x, a, out, name=None):
+        """One decode call (M <= 16) with h = A x inside the GEMV."""
         if comm is not None and name in ("o", "down"):
             _C.gemv_allreduce(comm, x, L.q_packed, L.lut_packed, out, L.N, L.K, 4, L.words_per_row,
-                              L.chunk_offsets, L.cols_packed, L.delta_packed, h, L.lora_B, L.dora_gamma,
-                              L.lora_scale, L.group_size, L.group_offset, _lib.WLQ_LUT_PREPACKED)
+                              L.chunk_offsets, L.cols_packed, L.delta_packed, None, L.lora_B, L.dora_gamma,
+                              L.lora_scale, L.group_size, L.group_offset, _lib.WLQ_LUT_PREPACKED, lora_A=a)
             return
+        rc = lib.wlq_gemv_lora_a(vp(L.q_packed), vp(L.lut_packed), vp(x), vp(out), vp(L.chunk_offsets),
+                                 vp(L.cols_packed), vp(L.delta_packed), vp(L.lora_B), vp(a), vp(L.dora_gamma),
+                                 L.lora_scale, L.r, x.shape[0], L.N, L.K, 4, L.words_per_row, L.group_size,
+                                 L.group_offset, _lib.WLQ_LUT_PREPACKED, _lib.WLQ_DTYPE_BF16,
+                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        _lib.check(rc, "wlq_gemv_lora_a")
+
+    def launch_gemm(L, x, h, out):
+        """One prefill call (M > 16) given h = A x."""
         rc = lib.wlq_gemm(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(L.q_packed.data_ptr()),
                           ctypes.c_void_p(L.lut_packed.data_ptr()), ctypes.c_void_p(out.data_ptr()),
                           ctypes.c_void_p(L.chunk_offsets.data_ptr()), ctypes.c_void_p(L.cols_packed.data_ptr()),
@@ -270,8 +282,8 @@ def run_ours(args):
 
     # eager warm-up (also loads the kernels) before capture
     for c in range(copies):
-        for (_, name, M, L, x, h, out) in per_copy[c]:
-            launch(L, x, h, out, name)
+        for (_, name, M, L, x, a, out) in per_copy[c]:
+            launch(L, x, a, out, name)
             reduce_if_rowpar(name, out)
     torch.cuda.synchronize()
 
@@ -283,10 +295,10 @@ def run_ours(args):
             with torch.cuda.graph(g, stream=s):
                 e = ev_base
                 for st in step_range:
-                    for (_, name, M, L, x, h, out) in per_copy[order[st]]:
+                    for (_, name, M, L, x, a, out) in per_copy[order[st]]:
                         if events:
                             ge.record(evs[e])
-                        launch(L, x, h, out, name)
+                        launch(L, x, a, out, name)
                         if events:
                             ge.record(evs[e + 1])
                         e += 2
@@ -321,7 +333,7 @@ def run_ours(args):
     per_cfg = {}
     e = 2 * 16 * args.warmup
     for st in range(args.warmup, steps_total):
-        for (_, name, M, L, x, h, out) in per_copy[order[st]]:
+        for (_, name, M, L, x, _a, out) in per_copy[order[st]]:
             d = evs[e].elapsed_time(evs[e + 1])  # kernel-only time of this launch
             b = L.algorithmic_bytes(M)
             kern_ms += d
@@ -350,7 +362,7 @@ def run_ours(args):
             n += (t.numel() * t.element_size() + 255) // 256 * 256
         return offs, n
 
-    ins = [t for (_, _, _, _, x, h, _) in per_copy[0] for t in (x, h)]
+    ins = [x for (_, _, _, _, x, _, _) in per_copy[0]]
     outs = [out for (*_r, out) in per_copy[0]]
     in_offs, in_n = arena(ins)
     out_offs, out_n = arena(outs)
@@ -365,23 +377,22 @@ def run_ours(args):
     for t, o in zip(ins, in_offs):
         view(in_host, o, t).copy_(t.cpu())
     host = []
-    for i, (c, name, M, L, x, h, out) in enumerate(per_copy[0]):
-        host.append((name, L, view(in_dev, in_offs[2 * i], x), view(in_dev, in_offs[2 * i + 1], h),
-                     view(out_dev, out_offs[i], out)))
+    for i, (c, name, M, L, x, a, out) in enumerate(per_copy[0]):
+        host.append((name, L, view(in_dev, in_offs[i], x), a, view(out_dev, out_offs[i], out)))
     h2d = sum(t.numel() * t.element_size() for t in ins)
     d2h = sum(t.numel() * t.element_size() for t in outs)
 
     def e2e_enqueue():
         in_dev.copy_(in_host, non_blocking=True)
-        for (name, L, xd, hd, od) in host:
+        for (name, L, xd, a, od) in host:
             if comm is not None and name in ("o", "down"):
                 _C.gemv_allreduce(comm, xd, L.q_packed, L.lut_packed, od, L.N, L.K, 4, L.words_per_row,
-                                  L.chunk_offsets, L.cols_packed, L.delta_packed, hd, L.lora_B, L.dora_gamma,
-                                  L.lora_scale, L.group_size, L.group_offset, 1)
+                                  L.chunk_offsets, L.cols_packed, L.delta_packed, None, L.lora_B, L.dora_gamma,
+                                  L.lora_scale, L.group_size, L.group_offset, 1, lora_A=a)
             else:
                 torch.ops.wlq_fastShot.gemm(xd, L.q_packed, L.lut_packed, od, L.N, L.K, 4, L.words_per_row,
-                                            L.chunk_offsets, L.cols_packed, L.delta_packed, hd, L.lora_B,
-                                            L.dora_gamma, L.lora_scale, L.group_size, L.group_offset, 1)
+                                            L.chunk_offsets, L.cols_packed, L.delta_packed, None, L.lora_B,
+                                            L.dora_gamma, L.lora_scale, L.group_size, L.group_offset, 1, a)
             reduce_if_rowpar(name, od)
         out_host.copy_(out_dev, non_blocking=True)
 
@@ -428,7 +439,7 @@ def run_ours(args):
     e2e_value = step_bytes_job * args.steps / (e2e_ms * 1e-3) / 1e9
     eager_value = step_bytes_job * args.steps / (eager_ms * 1e-3) / 1e9
 
-    gemm = gemm_leg(layers, dev, launch, peaks, peaks_kind, local) if world == 1 else None
+    gemm = gemm_leg(layers, dev, launch_gemm, peaks, peaks_kind, local) if world == 1 else None
 
     result = None
     if rank == 0:
@@ -458,13 +469,15 @@ def run_ours(args):
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "peak_source": f"{peaks_kind} hbm_gbs (MEASURED_PEAKS.json)" if peaks_kind == "measured"
                 else "fallback 6650 GB/s",
-                "kernel": "gemv_kernel (wlq_gemv.cu), all 16 (linear, M) launches of a step",
+                "kernel": "gemv_kernel with h = A x in the kernel (wlq_gemv_kernel.cuh), all 16 (linear, M) "
+                          "launches of a step",
                 "per_config_gbs": {k: round(v[1] / (v[0] * 1e-3) / 1e9, 1) for k, v in per_cfg.items()},
             },
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "path": "torch.ops.wlq_fastShot.gemm on every (linear, M) of a step; the step's activations "
-                            "copied from one pinned host buffer and its outputs read back into one, every step; "
+                    "path": "torch.ops.wlq_fastShot.gemm(..., lora_A) on every (linear, M) of a step (h = A x "
+                            "inside the GEMV); the step's activations copied from one pinned host buffer and its "
+                            "outputs read back into one, every step; "
                             "the step replayed as one CUDA graph (as vLLM runs decode), host synchronised per step",
                     "eager_value": round(eager_value, 1)},
             "gpu_launches": 16 * args.steps,
@@ -566,8 +579,8 @@ def _cpu_call(L, M, gen):
     import torch
     from oracle.cpu_baseline import cpu_forward
     x = torch.randn((M, L.K), generator=gen).to(torch.bfloat16)
-    h = torch.nn.functional.linear(x.float(), L.lora_A.float())
     t = time.perf_counter()
+    h = torch.nn.functional.linear(x.float(), L.lora_A.float())  # the reference's F.linear(x, A)
     cpu_forward(L.q_packed.numpy(), L.words_per_row, L.lut_c, L.N, L.K, GROUP, 0, L.chunk_offsets.numpy(),
                 L.chunk_cols.numpy().astype(np.int64), L.chunk_vals.numpy(), x.float(), h, L.lora_B, L.dora_gamma,
                 L.lora_scale)
@@ -650,13 +663,21 @@ def run_case(args):
     x = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)
     hs = [S.lora_h(L, x) for L in layers]
     out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+
+    def call(i):  # decode: h = A x inside the GEMV; prefill: h given
+        L = layers[i % len(layers)]
+        if M <= 16:
+            S.forward_fold(L, x, out)
+        else:
+            S.forward(L, x, out, hs[i % len(layers)])
+
     for i in range(args.warmup):
-        S.forward(layers[i % len(layers)], x, out, hs[i % len(layers)])
+        call(i)
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for i in range(args.steps):
-        S.forward(layers[i % len(layers)], x, out, hs[i % len(layers)])
+        call(i)
     t1.record()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / args.steps

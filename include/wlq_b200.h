@@ -90,6 +90,18 @@ WLQ_API int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, 
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
              int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
 
+/* wlq_gemv with the DoRA low-rank input computed inside the kernel: lora_A
+ * ([r, K] in act_dtype, r <= 32) takes the place of lora_h = A x.  Needs
+ * WLQ_LUT_PREPACKED and 16-byte aligned rows of x and lora_A (K % 8 == 0).
+ * Folds the two launches that precede every reference GEMV,
+ * F.linear(x, lora_A).float() (vllm_wlq/linear_method.py:962-963), into the
+ * GEMV; h is kept in fp32 instead of being rounded to fp16 first. */
+WLQ_API int wlq_gemv_lora_a(const int32_t* q_packed, const void* lut_c, const void* x, void* out,
+             const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
+             const void* lora_B, const void* lora_A, const void* dora_gamma, float lora_scale,
+             int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
+             int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
+
 /* Batched forward for any M >= 1: M <= 16 runs the GEMV-class kernel, larger
  * M the tcgen05 tensor-core GEMM with dequantisation, outlier replacement and
  * the DoRA epilogue fused.  chunk_cols / chunk_vals: uint16 columns and e5m2
@@ -162,10 +174,13 @@ WLQ_API int wlq_tp_buffer_free(void* ptr);
 WLQ_API int wlq_tp_error(void* local_buf, unsigned int* flags_out, int clear);
 /* wlq_gemv (M <= 16) on this rank's K shard with the all-reduce of out over
  * the tp_world ranks fused; tp_bufs[q] is rank q's buffer as mapped in this
- * process (tp_bufs[tp_rank] the local one), max_N the N it was sized for. */
+ * process (tp_bufs[tp_rank] the local one), max_N the N it was sized for.
+ * The DoRA input is lora_h, or lora_A (this rank's K columns of A) as in
+ * wlq_gemv_lora_a; the other one is null. */
 WLQ_API int wlq_gemv_allreduce(const int32_t* q_packed, const void* lut_c, const void* x, void* out,
              const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
-             const void* lora_B, const float* lora_h, const void* dora_gamma, float lora_scale,
+             const void* lora_B, const float* lora_h, const void* lora_A, const void* dora_gamma,
+             float lora_scale,
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
              int lut_group_offset, int lut_format, int act_dtype, void* const* tp_bufs, int tp_rank,
              int tp_world, int max_N, wlq_stream_t stream);

@@ -68,7 +68,7 @@ def _check_opt(name, nm, t, dtype, device):
 
 
 def _linear_checks(name, x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lora_B, lora_h, gamma,
-                   group_size, group_offset, lut_format=WLQ_LUT_F16):
+                   group_size, group_offset, lut_format=WLQ_LUT_F16, lora_A=None):
     _check_common(name, (q_packed, lut_c, x, out), ("q_packed", "lut_c", "x", "out"))
     _require(bits == 4, f"{name}: the fused kernels read 4-bit indices only (bits={bits})")
     dev = x.device
@@ -96,14 +96,19 @@ def _linear_checks(name, x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, v
         _require(offs.numel() == N * (nc + 1), f"{name}: chunk_offsets must be [{N}, {nc + 1}]")
         _require(cols.numel() == vals.numel(), f"{name}: chunk_cols and chunk_vals lengths differ")
     r = 0
-    if lora_B is not None and lora_h is not None and gamma is not None:
+    _require(lora_h is None or lora_A is None, f"{name}: give lora_h or lora_A, not both")
+    if lora_B is not None and (lora_h is not None or lora_A is not None) and gamma is not None:
         _check_opt(name, "lora_B", lora_B, torch.float16, dev)
-        _check_opt(name, "lora_h", lora_h, torch.float32, dev)
         _check_opt(name, "dora_gamma", gamma, torch.float16, dev)
         r = int(lora_B.size(1)) if lora_B.dim() > 1 else 0
         _require(lora_B.numel() == N * r, f"{name}: lora_B must be [{N}, r]")
-        _require(lora_h.numel() == M * r, f"{name}: lora_h must hold {M}x{r} values")
         _require(gamma.numel() == N, f"{name}: dora_gamma must have {N} values")
+        if lora_h is not None:
+            _check_opt(name, "lora_h", lora_h, torch.float32, dev)
+            _require(lora_h.numel() == M * r, f"{name}: lora_h must hold {M}x{r} values")
+        else:
+            _check_opt(name, "lora_A", lora_A, x.dtype, dev)  # A in the activation type
+            _require(lora_A.numel() == r * K, f"{name}: lora_A must be [{r}, {K}]")
     return M, r
 
 
@@ -150,6 +155,25 @@ def gemv_forward(q_packed, lut_c, x, out, N, K, bits, chunk_offsets=None, chunk_
     check(rc, "wlq_gemv")
 
 
+def gemv_lora_a(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_A,
+                dora_gamma, lora_scale=1.0, lut_group_size=0, lut_group_offset=0, lut_format=WLQ_LUT_PREPACKED):
+    """Decode GEMV (M <= 16) that computes the DoRA input h = lora_A x itself
+    (lora_A [r, K] in x's dtype, r <= 32; prepacked layout): one launch in
+    place of F.linear + .float() + GEMV (vllm_wlq/linear_method.py:962-999)."""
+    N, K, bits = int(N), int(K), int(bits)
+    offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
+    lb, la, gm = _opt(lora_B), _opt(lora_A), _opt(dora_gamma)
+    wpr = words_per_row(K, bits)
+    M, r = _linear_checks("gemv_lora_a", x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lb, None, gm,
+                          int(lut_group_size), int(lut_group_offset), int(lut_format), lora_A=la)
+    with _DeviceGuard(x.device):
+        rc = lib.wlq_gemv_lora_a(_ptr(q_packed), _ptr(lut_c), _ptr(x), _ptr(out), _ptr(offs), _ptr(cols),
+                                 _ptr(vals), _ptr(lb), _ptr(la), _ptr(gm), float(lora_scale), r, M, N, K, bits, wpr,
+                                 int(lut_group_size), int(lut_group_offset), int(lut_format), _act_dtype(x),
+                                 _stream(x.device))
+    check(rc, "wlq_gemv_lora_a")
+
+
 def gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,
                  chunk_vals=None, lora_H=None, lora_B=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
                  lut_group_offset=0, lut_format=WLQ_LUT_F16):
@@ -169,21 +193,23 @@ def gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offse
 
 def gemv_allreduce(comm, X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,
                    chunk_vals=None, lora_H=None, lora_B=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
-                   lut_group_offset=0, lut_format=WLQ_LUT_F16):
+                   lut_group_offset=0, lut_format=WLQ_LUT_F16, lora_A=None):
     """Row-parallel decode forward (M <= 16) on this rank's K shard with the
     all-reduce of `out` over `comm`'s ranks fused into the kernel (see
-    qwen_wlqfastshot_helen_beta_b200.tp.TPComm).  Every rank of the group
-    must make the same calls in the same order."""
+    qwen_wlqfastshot_helen_beta_b200.tp.TPComm).  The DoRA input is lora_H,
+    or lora_A (this rank's K columns of A, computed into h in the kernel as in
+    gemv_lora_a).  Every rank of the group must make the same calls in the
+    same order."""
     N, K, bits, wpr = int(N), int(K), int(bits), int(words_per_row)
     offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
-    lb, lh, gm = _opt(lora_B), _opt(lora_H), _opt(dora_gamma)
+    lb, lh, la, gm = _opt(lora_B), _opt(lora_H), _opt(lora_A), _opt(dora_gamma)
     M, r = _linear_checks("gemv_allreduce", X, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lb, lh, gm,
-                          int(lut_group_size), int(lut_group_offset), int(lut_format))
+                          int(lut_group_size), int(lut_group_offset), int(lut_format), lora_A=la)
     with _DeviceGuard(X.device):
         rc = lib.wlq_gemv_allreduce(_ptr(q_packed), _ptr(lut_c), _ptr(X), _ptr(out), _ptr(offs), _ptr(cols),
-                                    _ptr(vals), _ptr(lb), _ptr(lh), _ptr(gm), float(lora_scale), r, M, N, K, bits,
-                                    wpr, int(lut_group_size), int(lut_group_offset), int(lut_format), _act_dtype(X),
-                                    comm.bufs, comm.rank, comm.world, comm.max_N, _stream(X.device))
+                                    _ptr(vals), _ptr(lb), _ptr(lh), _ptr(la), _ptr(gm), float(lora_scale), r, M, N,
+                                    K, bits, wpr, int(lut_group_size), int(lut_group_offset), int(lut_format),
+                                    _act_dtype(X), comm.bufs, comm.rank, comm.world, comm.max_N, _stream(X.device))
     check(rc, "wlq_gemv_allreduce")
 
 

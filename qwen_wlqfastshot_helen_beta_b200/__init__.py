@@ -2,9 +2,11 @@
 
 Drop-in for the reference plugin's hot path (vllm_wlq/__init__.py:1-90):
 the same ``torch.ops.wlq_fastShot.gemv`` / ``torch.ops.wlq_fastShot.gemm``
-custom ops (same schema, ``out`` mutated, fake implementations for CUDA-graph
-capture and torch.compile), ``init_workspaces`` and the ``register`` vLLM
-plugin entry point.  ``WLQFastShotConfig`` / ``WLQLinearMethod`` import vLLM
+custom ops (the reference schema with optional trailing arguments for
+per-group codebooks, the prepacked layout and ``lora_A``, the DoRA matrix A
+given in place of h = A x so the decode GEMV computes h itself; ``out``
+mutated, fake implementations for CUDA-graph capture and torch.compile),
+``init_workspaces`` and the ``register`` vLLM plugin entry point.  ``WLQFastShotConfig`` / ``WLQLinearMethod`` import vLLM
 and are loaded on first access.
 """
 from __future__ import annotations
@@ -38,14 +40,19 @@ def _register_ops():
         lut_group_size: int = 0,
         lut_group_offset: int = 0,
         lut_format: int = 0,
+        lora_A: Optional[torch.Tensor] = None,
     ) -> None:
+        if lora_A is not None and lora_h is None:  # h = A x inside the GEMV
+            _C.gemv_lora_a(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
+                           lora_A, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
+            return
         _C.gemv_forward(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
                         lora_h, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
 
     @_gemv_op.register_fake
     def _gemv_fake(q_packed, lut_c, x, out, N, K, bits, chunk_offsets=None, chunk_cols=None, chunk_vals=None,
                    lora_B=None, lora_h=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
-                   lut_group_offset=0, lut_format=0):
+                   lut_group_offset=0, lut_format=0, lora_A=None):
         return None
 
     @torch.library.custom_op("wlq_fastShot::gemm", mutates_args={"out"})
@@ -68,7 +75,16 @@ def _register_ops():
         lut_group_size: int = 0,
         lut_group_offset: int = 0,
         lut_format: int = 0,
+        lora_A: Optional[torch.Tensor] = None,
     ) -> None:
+        if lora_A is not None and lora_H is None:
+            M = X.numel() // int(K)
+            if M <= 16:  # h = A x inside the GEMV: one launch
+                _C.gemv_lora_a(q_packed, lut_c, X, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
+                               lora_A, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
+                return
+            # prefill: h = A x as one library GEMM, as the reference computes it
+            lora_H = torch.nn.functional.linear(X.reshape(M, int(K)), lora_A).float()
         _C.gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets, chunk_cols,
                         chunk_vals, lora_H, lora_B, dora_gamma, lora_scale, lut_group_size, lut_group_offset,
                         lut_format)
@@ -76,7 +92,7 @@ def _register_ops():
     @_gemm_op.register_fake
     def _gemm_fake(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,
                    chunk_vals=None, lora_H=None, lora_B=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
-                   lut_group_offset=0, lut_format=0):
+                   lut_group_offset=0, lut_format=0, lora_A=None):
         return None
 
 

@@ -27,6 +27,8 @@ SIGNATURES = {
     "wlq_abi_version": (_i32, []),
     "wlq_gemv": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
                         _i32, _i32, _i32, _i32, _p]),
+    "wlq_gemv_lora_a": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
+                               _i32, _i32, _i32, _i32, _p]),
     "wlq_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
                         _i32, _i32, _i32, _i32, _p]),
     "wlq_prepack_lut": (_i32, [_p, _p, _i64, _i32, _p]),
@@ -42,8 +44,9 @@ SIGNATURES = {
     "wlq_tp_buffer_close": (_i32, [_p]),
     "wlq_tp_buffer_free": (_i32, [_p]),
     "wlq_tp_error": (_i32, [_p, ctypes.POINTER(ctypes.c_uint), _i32]),
-    "wlq_gemv_allreduce": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
-                                  _i32, _i32, _i32, _i32, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i32, _p]),
+    "wlq_gemv_allreduce": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32,
+                                  _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _i32,
+                                  _p]),
     "wlq_words_per_row": (_i64, [_i64, _i32]),
     "wlq_repack_q_indices_row_aligned": (_i32, [_p, _i64, _i64, _i64, _i32, _p, _i64, _p64]),
     "wlq_repack_q_indices_slice": (_i32, [_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i64, _p, _i64, _p64]),

@@ -58,10 +58,13 @@ int require_sm100() {
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Shared validation of the quantized-linear arguments.
+// lorah (the low-rank input h = A x, fp32 [M, r]) or loraA (A itself, [r, K]
+// in act_dtype, for the GEMV to compute h) carries the DoRA input; at most one
+// of them is given.
 int build_args(const char* fn, const void* x, const int32_t* q, const void* lut, void* out,
                const int32_t* off, const void* ccols, const void* cvals, const void* loraB,
-               const float* lorah, const void* gamma, float scale, int r, int M, int N, int K, int bits,
-               int wpr, int G, int goff, int lut_format, int dtype, LinearArgs& a) {
+               const float* lorah, const void* loraA, const void* gamma, float scale, int r, int M, int N, int K,
+               int bits, int wpr, int G, int goff, int lut_format, int dtype, LinearArgs& a) {
     if (M < 0 || N < 0 || K < 0) return fail(WLQ_ERR_INVALID_ARG, "%s: negative size (M=%d N=%d K=%d)", fn, M, N, K);
     if (bits != 4)
         return fail(WLQ_ERR_UNSUPPORTED, "%s: only 4-bit indices are supported by the fused kernels (bits=%d)", fn, bits);
@@ -84,7 +87,8 @@ int build_args(const char* fn, const void* x, const int32_t* q, const void* lut,
     const bool has_outl = off && ccols && cvals;
     if (has_outl && lut_format == WLQ_LUT_PREPACKED && K > 65535)
         return fail(WLQ_ERR_UNSUPPORTED, "%s: prepacked outliers hold uint16 columns; K=%d is too large", fn, K);
-    const bool dora = loraB && lorah && gamma && r > 0;
+    if (lorah && loraA) return fail(WLQ_ERR_INVALID_ARG, "%s: give lora_h or lora_A, not both", fn);
+    const bool dora = loraB && (lorah || loraA) && gamma && r > 0;
     a.q = reinterpret_cast<const uint32_t*>(q);
     a.lut = reinterpret_cast<const uint16_t*>(lut);
     a.x = x;
@@ -94,6 +98,7 @@ int build_args(const char* fn, const void* x, const int32_t* q, const void* lut,
     a.cvals = has_outl ? cvals : nullptr;
     a.loraB = dora ? reinterpret_cast<const uint16_t*>(loraB) : nullptr;
     a.lorah = dora ? lorah : nullptr;
+    a.loraA = dora ? reinterpret_cast<const uint16_t*>(loraA) : nullptr;
     a.gamma = dora ? reinterpret_cast<const uint16_t*>(gamma) : nullptr;
     a.scale = scale;
     a.r = dora ? r : 0;
@@ -135,10 +140,27 @@ int wlq_gemv(const int32_t* q_packed, const void* lut_c, const void* x, void* ou
     g_last_error[0] = '\0';
     LinearArgs a;
     int rc = build_args("wlq_gemv", x, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_h,
-                        dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size, lut_group_offset,
+                        nullptr, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size, lut_group_offset,
                         lut_format, act_dtype, a);
     if (rc) return rc;
     if (M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: M must be 1..16 (got %d); use wlq_gemm", M);
+    if (M == 0 || N == 0) return WLQ_OK;
+    if ((rc = require_sm100())) return rc;
+    return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wlq_gemv_lora_a(const int32_t* q_packed, const void* lut_c, const void* x, void* out,
+                    const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals, const void* lora_B,
+                    const void* lora_A, const void* dora_gamma, float lora_scale, int r, int M, int N, int K, int bits,
+                    int words_per_row, int lut_group_size, int lut_group_offset, int lut_format, int act_dtype,
+                    wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    LinearArgs a;
+    int rc = build_args("wlq_gemv_lora_a", x, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B,
+                        nullptr, lora_A, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size,
+                        lut_group_offset, lut_format, act_dtype, a);
+    if (rc) return rc;
+    if (M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_lora_a: M must be 1..16 (got %d)", M);
     if (M == 0 || N == 0) return WLQ_OK;
     if ((rc = require_sm100())) return rc;
     return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
@@ -151,7 +173,7 @@ int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* ou
     g_last_error[0] = '\0';
     LinearArgs a;
     int rc = build_args("wlq_gemm", X, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_H,
-                        dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size, lut_group_offset,
+                        nullptr, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size, lut_group_offset,
                         lut_format, act_dtype, a);
     if (rc) return rc;
     if (M == 0 || N == 0) return WLQ_OK;
@@ -298,14 +320,14 @@ int wlq_tp_error(void* local_buf, unsigned int* flags_out, int clear) {
 
 int wlq_gemv_allreduce(const int32_t* q_packed, const void* lut_c, const void* x, void* out,
                        const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
-                       const void* lora_B, const float* lora_h, const void* dora_gamma, float lora_scale, int r,
-                       int M, int N, int K, int bits, int words_per_row, int lut_group_size, int lut_group_offset,
-                       int lut_format, int act_dtype, void* const* tp_bufs, int tp_rank, int tp_world, int max_N,
-                       wlq_stream_t stream) {
+                       const void* lora_B, const float* lora_h, const void* lora_A, const void* dora_gamma,
+                       float lora_scale, int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
+                       int lut_group_offset, int lut_format, int act_dtype, void* const* tp_bufs, int tp_rank,
+                       int tp_world, int max_N, wlq_stream_t stream) {
     g_last_error[0] = '\0';
     LinearArgs a;
     int rc = build_args("wlq_gemv_allreduce", x, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B,
-                        lora_h, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size,
+                        lora_h, lora_A, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size,
                         lut_group_offset, lut_format, act_dtype, a);
     if (rc) return rc;
     if (M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_allreduce: M must be 1..16 (got %d)", M);

@@ -33,536 +33,21 @@
 // its tile (the arithmetic of csrc/gemv_kernel.cu:262-288): two lanes per row
 // walk the row's chunk-CSR entries, accumulate in registers and combine with
 // one shuffle.
-#include "wlq_common.cuh"
-#include "wlq_internal.h"
+#include "wlq_gemv_kernel.cuh"
 
 namespace wlq {
 
+using namespace gemv;
+
 namespace {
-
-constexpr int kWarps = 4;
-constexpr int kRowsPerTile = 16;
-constexpr int kChunk = 128;  // k columns per warp iteration
-constexpr int kMaxTp = 8;    // ranks of a fused all-reduce
-
-struct GemvParams {
-    const uint32_t* q;
-    const uint16_t* lut;
-    const void* x;
-    void* out;
-    const int32_t* off;
-    const void* ccols;  // uint16 chunk-local columns, or uint32 records (prepacked)
-    const void* cvals;  // e5m2 bytes, or float32 corrections (prepacked)
-    const uint16_t* loraB;
-    const float* lorah;
-    const uint16_t* gamma;
-    float scale;
-    int r, M, N, K, wpr, G, goff, ngroups, chunk_m, ncsr;
-    int log2G;             // group_size = 1 << log2G when grouped
-    int kchunks;           // ceil(K / 128)
-    int chunks_per_rank;   // K split across the cluster
-    int x_stride;          // shared-memory row stride of staged activations (elements)
-    int x_bytes;           // bytes of dynamic shared memory before the ring (staged activations)
-    uint32_t mul16, mul31; // 1<<16 and 1<<31, runtime values so mul.hi stays a multiply
-    // fused tensor-parallel all-reduce (row-parallel layers), tp_world > 1
-    int tp_world, tp_rank, tp_nmax;
-    float* tp_data[kMaxTp];      // each rank's slots [2 parities][world][16 tokens][tp_nmax] fp32
-    uint32_t* tp_flags[kMaxTp];  // each rank's per-tile epochs [tiles][world]
-    uint32_t* tp_counters;       // this rank's per-tile call counters [tiles]
-    uint32_t* tp_err;            // this rank's error word
-};
-
-// Codebook value of symbol q of one (row, group) as the MMA saw it.
-template <typename T, bool PREPACKED>
-__device__ __forceinline__ float codebook_value(const uint16_t* __restrict__ lut, int64_t entry, uint32_t q) {
-    if (PREPACKED) {
-        const uint8_t* rec = reinterpret_cast<const uint8_t*>(lut + entry * 16);
-        const uint16_t bits = (uint16_t)(__ldg(rec + q) | ((uint16_t)__ldg(rec + 16 + q) << 8));
-        return ActTraits<T>::bits_to_f32(bits);
-    }
-    return ActTraits<T>::bits_to_f32(ActTraits<T>::from_f16_bits(__ldg(lut + entry * 16 + q)));
-}
-
-// Issues the staging of x[0:M, kb:kb+cols) into shared memory as one
-// cp.async group (the caller waits for it), rows padded by 8 elements (16
-// bytes) so the per-token rows fall in different banks; columns past K read
-// as zero.  16-byte cp.async when rows of x are 16-byte aligned.
-template <typename T, bool XVEC>
-__device__ __forceinline__ void stage_x_issue(uint16_t* xs, const T* __restrict__ x, int M, int K, int kb, int cols,
-                                              int stride) {
-    const uint16_t* xg = reinterpret_cast<const uint16_t*>(x);
-    const int pieces = cols / 8;
-    for (int e = threadIdx.x; e < M * pieces; e += blockDim.x) {
-        const int m = e / pieces, pc = e - m * pieces;
-        const int k = kb + 8 * pc;
-        uint16_t* dst = xs + m * stride + 8 * pc;
-        if (XVEC && k + 8 <= K) {
-            const uint32_t sa = smem_u32(dst);
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(xg + (int64_t)m * K + k) : "memory");
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) dst[j] = k + j < K ? xg[(int64_t)m * K + k + j] : (uint16_t)0;
-        }
-    }
-    cp_async_commit();
-}
-
-// Sum over the cluster's ranks of one partial-tile element, rank 0 first:
-// the remote loads are all issued before the adds.
-__device__ __forceinline__ float cluster_sum(const float* own, uint32_t nranks) {
-    if (nranks == 1) return *own;
-    const uint32_t a = smem_u32(own);
-    float v[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) v[q] = (uint32_t)q < nranks ? ld_shared_cluster_f32(mapa_shared(a, (uint32_t)q)) : 0.f;
-    float s = v[0];
-#pragma unroll
-    for (int q = 1; q < 8; ++q) s += v[q];
-    return s;
-}
-
-// Per-warp shared-memory ring of S stages, filled by cp.async (no register
-// scoreboards held by prefetches).  A stage holds one 128-column chunk: the
-// index words of the warp's 16 rows (16 x 64 B) and, with per-group
-// codebooks, NSLOT codebooks per row (16 x NSLOT x 32 B), slot s holding group
-// g0 + s where g0 is the group of the chunk's first column.
-template <int NSLOT>
-struct Ring {
-    static constexpr int kIdxBytes = kRowsPerTile * 64;
-    static constexpr int kPlaneBytes = kRowsPerTile * NSLOT * 32;
-    static constexpr int kStageBytes = kIdxBytes + kPlaneBytes;
-};
-
-__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
-    return v;
-}
-
-// Row-parallel epilogue with the all-reduce fused, for one warp's 16-row
-// tile (cluster rank 0): the tile's gamma-scaled partial results are pushed
-// into slot [parity][this rank] of every rank's buffer over NVLink peer
-// stores, the tile's epoch is published to every rank with a system-scope
-// release store, and once every rank's epoch for the tile has arrived
-// (bounded wait) the local slots are summed into out.  Epochs come from a
-// per-tile call counter that advances identically on every rank, so CUDA
-// graph replays need no host input; slots alternate by epoch parity, and a
-// rank cannot run two calls ahead on a tile because each call waits for all
-// ranks' data of the previous one.
-template <typename T, int MT>
-__device__ void tp_allreduce_tile(const GemvParams& p, float (*part)[MT], uint32_t nranks, int tile_row0, int lane,
-                                  float gam) {
-    const int tile = tile_row0 / kRowsPerTile;
-    const int world = p.tp_world, me = p.tp_rank;
-    const bool clustered = nranks > 1;
-    uint32_t cnt = lane == 0 ? p.tp_counters[tile] + 1u : 0u;
-    cnt = __shfl_sync(0xFFFFFFFFu, cnt, 0);
-    const int par = (int)(cnt & 1u);
-    for (int e = lane; e < kRowsPerTile * MT; e += 32) {
-        const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
-        const int n = tile_row0 + rl;
-        if (n >= p.N || tk >= p.M) continue;
-        const float s = cluster_sum(&part[rl][tk], clustered ? nranks : 1u) * gam;
-        const int64_t slot = ((int64_t)(par * world + me) * kRowsPerTile + tk) * p.tp_nmax + n;
-        for (int q = 0; q < world; ++q) p.tp_data[q][slot] = s;
-    }
-    __threadfence_system();  // this lane's peer stores before the epoch
-    __syncwarp();
-    int ok = 1;
-    if (lane == 0) {
-        for (int q = 0; q < world; ++q) st_release_sys(p.tp_flags[q] + tile * world + me, cnt);
-        const uint32_t* mine = p.tp_flags[me] + tile * world;
-        const uint64_t t0 = globaltimer_ns();
-        for (int q = 0; q < world && ok; ++q) {
-            while (ld_acquire_sys(mine + q) < cnt) {
-                if (globaltimer_ns() - t0 > 2000000000ull) {  // a rank never arrived: give up
-                    atomicOr(p.tp_err, 1u);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        p.tp_counters[tile] = cnt;
-    }
-    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-    __threadfence();
-    if (!ok) return;
-    for (int e = lane; e < kRowsPerTile * MT; e += 32) {
-        const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
-        const int n = tile_row0 + rl;
-        if (n >= p.N || tk >= p.M) continue;
-        float s = 0.f;
-        for (int q = 0; q < world; ++q)
-            s += __ldcg(p.tp_data[me] + ((int64_t)(par * world + q) * kRowsPerTile + tk) * p.tp_nmax + n);
-        reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s);
-    }
-}
-
-template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int S>
-__global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p) {
-    constexpr bool GROUPED = NSLOT > 0;
-    constexpr int MT = 8 * NT;
-    using R = Ring<NSLOT>;
-    static_assert(S >= 2, "ring needs two stages");
-    extern __shared__ __align__(128) uint8_t smem[];  // [x stage (XSMEM)][kWarps][S] ring stages
-    __shared__ float part[kWarps][kRowsPerTile][MT];  // per-warp partial tile
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int g = lane >> 2;
-    const int t = lane & 3;
-    const int tile_row0 = (blockIdx.x * kWarps + warp) * kRowsPerTile;
-    const int row0 = tile_row0 + g;
-    const bool v0 = row0 < p.N;
-    const bool v1 = row0 + 8 < p.N;
-    const T* x = reinterpret_cast<const T*>(p.x);
-    const uint32_t m16 = p.mul16, m31 = p.mul31;
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem);  // [M][x_stride] activations of this rank's K range
-    const uint32_t ring = smem_u32(smem + p.x_bytes) + (uint32_t)(warp * S * R::kStageBytes);
-
-    const int c_begin = blockIdx.y * p.chunks_per_rank;
-    const int c_end = min(p.kchunks, c_begin + p.chunks_per_rank);
-
-    // codebook group of a column (clamped: columns past K meet zero activations)
-    auto group_at = [&](int col) { return min((col + p.goff) >> p.log2G, p.ngroups - 1); };
-
-    // chunk c into ring stage st; one commit group per lane per chunk, empty
-    // past the rank's range
-    auto issue = [&](int c, int st) {
-        if (c < c_end) {
-            const uint32_t base = ring + (uint32_t)(st * R::kStageBytes);
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int pc = lane + 32 * i;
-                const int r = pc >> 2, q4 = pc & 3;
-                const int row = tile_row0 + r;
-                const int wi = c * (kChunk / 8) + 4 * q4;
-                const bool ok = row < p.N && wi < p.wpr;
-                cp_async16(base + r * 64 + q4 * 16, p.q + (ok ? (int64_t)row * p.wpr + wi : 0), ok);
-            }
-            if constexpr (GROUPED) {
-                const int g0 = group_at(c * kChunk);
-                const int used = group_at(c * kChunk + kChunk - 1) - g0 + 1;
-#pragma unroll
-                for (int i = 0; i < NSLOT; ++i) {
-                    const int pc = lane + 32 * i;
-                    const int r = pc / (2 * NSLOT), s = (pc >> 1) % NSLOT, half = pc & 1;
-                    const int row = tile_row0 + r;
-                    const bool ok = row < p.N && s < used;
-                    cp_async16(base + R::kIdxBytes + (r * NSLOT + s) * 32 + half * 16,
-                               p.lut + (ok ? ((int64_t)row * p.ngroups + g0 + s) * 16 + 8 * half : 0), ok);
-                }
-            }
-        }
-        cp_async_commit();
-    };
-#pragma unroll
-    for (int j = 0; j < S - 1; ++j) issue(c_begin + j, j);
-    // this rank's activations into shared memory (XSMEM), waited for after
-    // the low-rank MMA; larger slices are read through L1
-    const int kb0 = c_begin * kChunk;
-    if (XSMEM) stage_x_issue<T, XVEC>(xs, x, p.M, p.K, kb0, p.chunks_per_rank * kChunk, p.x_stride);
-
-    // per-row codebooks (no grouping) stay in registers for the whole K range
-    LutPlanes PR0, PR1;
-    if (!GROUPED) {
-        load_planes<T, PREPACKED>(p.lut, row0, v0, PR0);
-        load_planes<T, PREPACKED>(p.lut, row0 + 8, v1, PR1);
-    }
-
-    float acc[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
-
-    // this row's outlier range (prepacked layout), loaded before the
-    // activation staging wait so the latency overlaps it
-    const bool o_has = p.off != nullptr && c_begin < c_end && tile_row0 + (lane & 15) < p.N;
-    int o_ia = 0, o_ib = 0;
-    if (PREPACKED && o_has) {
-        const int32_t* ro = p.off + (int64_t)(tile_row0 + (lane & 15)) * (p.ncsr + 1);
-        o_ia = __ldg(ro + c_begin * kChunk / p.chunk_m);
-        o_ib = __ldg(ro + (min(p.K, c_end * kChunk) - 1) / p.chunk_m + 1);
-    }
-    // DoRA magnitude of the row this lane finishes in the epilogue
-    const int erow = tile_row0 + (lane & 15);
-    const float gam = (p.r > 0 && erow < p.N) ? f16_bits_to_f32(__ldg(p.gamma + erow)) : 1.f;
-
-    // DoRA low-rank term s * B h on the tensor core, once per output tile
-    // (cluster rank 0), into the accumulators before the main loop: A = the
-    // tile's 16 rows of B (k = rank index), the B operand = s * h per token,
-    // both rounded to the MMA type
-    if (p.r > 0 && (gridDim.y == 1 || cluster_ctarank() == 0u)) {
-        const uint16_t* B0 = p.loraB + (int64_t)(v0 ? row0 : 0) * p.r;
-        const uint16_t* B1 = p.loraB + (int64_t)(v1 ? row0 + 8 : 0) * p.r;
-        auto bval = [&](const uint16_t* Br, bool ok, int k) -> uint32_t {  // one 16-bit element
-            return (ok && k < p.r) ? (uint32_t)ActTraits<T>::from_f16_bits(__ldg(Br + k)) : 0u;
-        };
-        for (int kb = 0; kb < p.r; kb += 16) {
-            uint32_t a[4];
-            const int k0 = kb + 2 * t, k8 = kb + 2 * t + 8;
-            a[0] = bval(B0, v0, k0) | (bval(B0, v0, k0 + 1) << 16);
-            a[1] = bval(B1, v1, k0) | (bval(B1, v1, k0 + 1) << 16);
-            a[2] = bval(B0, v0, k8) | (bval(B0, v0, k8 + 1) << 16);
-            a[3] = bval(B1, v1, k8) | (bval(B1, v1, k8 + 1) << 16);
-#pragma unroll
-            for (int tt = 0; tt < NT; ++tt) {
-                const int tok = 8 * tt + g;
-                const float* h = p.lorah + (int64_t)(tok < p.M ? tok : 0) * p.r;
-                auto hv = [&](int k) { return (tok < p.M && k < p.r) ? p.scale * __ldg(h + k) : 0.f; };
-                const T h0 = ActTraits<T>::from_f32(hv(k0)), h1 = ActTraits<T>::from_f32(hv(k0 + 1));
-                const T h8 = ActTraits<T>::from_f32(hv(k8)), h9 = ActTraits<T>::from_f32(hv(k8 + 1));
-                const uint32_t b0 = (uint32_t)*reinterpret_cast<const uint16_t*>(&h0) |
-                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(&h1) << 16);
-                const uint32_t b1 = (uint32_t)*reinterpret_cast<const uint16_t*>(&h8) |
-                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(&h9) << 16);
-                Mma16816<T>::run(acc[tt], a, b0, b1);
-            }
-        }
-    }
-
-    // this lane's first outlier entries (prepacked layout: global columns
-    // and ready corrections), loaded before the activation wait; lanes l and
-    // l+16 take alternate entries of row l % 16, four in flight per lane
-    const uint32_t* orec = reinterpret_cast<const uint32_t*>(p.ccols);
-    const float* odel = reinterpret_cast<const float*>(p.cvals);
-    int ocol[4];
-    float odl[4];
-    auto load_outliers = [&](int i0, int ib) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = i0 + 2 * u;
-            ocol[u] = i < ib ? (int)(__ldg(orec + i) & 0xFFFFu) : -1;
-            odl[u] = i < ib ? __ldg(odel + i) : 0.f;
-        }
-    };
-    if (PREPACKED && o_has) load_outliers(o_ia + (lane >> 4), o_ib);
-    if (XSMEM) {
-        cp_async_wait<0>();  // the staged activations (and the ring's first chunks)
-        __syncthreads();
-    }
-    bool tok_ok[NT];
-    const uint16_t* xrow[NT];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-        tok_ok[j] = 8 * j + g < p.M;
-        const int tok = tok_ok[j] ? 8 * j + g : 0;
-        xrow[j] = XSMEM ? xs + tok * p.x_stride + 32 * t  // this lane's 32 columns of chunk c_begin
-                        : reinterpret_cast<const uint16_t*>(x) + (int64_t)tok * p.K + kb0 + 32 * t;
-    }
-
-    // activations run one k-step pair ahead of their use
-    auto lds_x8 = [&](int tt, int off) -> uint4 {
-        if (!tok_ok[tt]) return make_uint4(0u, 0u, 0u, 0u);
-        const int k = kb0 + 32 * t + off;  // global column of this 8-wide piece
-        if constexpr (XSMEM) {
-            return *reinterpret_cast<const uint4*>(xrow[tt] + off);
-        } else if constexpr (XVEC) {
-            return k + 8 <= p.K ? ldg_keep_v4(xrow[tt] + off) : make_uint4(0u, 0u, 0u, 0u);
-        } else {
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t lo = k + 2 * j < p.K ? (uint32_t)__ldg(xrow[tt] + off + 2 * j) : 0u;
-                const uint32_t hi = k + 2 * j + 1 < p.K ? (uint32_t)__ldg(xrow[tt] + off + 2 * j + 1) : 0u;
-                w[j] = lo | (hi << 16);
-            }
-            return make_uint4(w[0], w[1], w[2], w[3]);
-        }
-    };
-    auto x_at = [&](int m, int col) -> float {  // activation of token m at global column col
-        return XSMEM ? ActTraits<T>::bits_to_f32(xs[m * p.x_stride + col - kb0])
-                     : ActTraits<T>::to_f32(x[(int64_t)m * p.K + col]);
-    };
-    // outlier replacement over this rank's K range, done before the main
-    // loop so its dependent loads overlap the ring fill instead of trailing
-    // it: lanes l and l+16 share tile row l % 16 and take alternate entries
-    // of its chunk-CSR range; the sums seed the warp's partial tile
-    {
-        const int kb = c_begin * kChunk;
-        const int ke = min(p.K, c_end * kChunk);
-        const int rl = lane & 15;
-        const int row = tile_row0 + rl;
-        float os[MT];
-#pragma unroll
-        for (int m = 0; m < MT; ++m) os[m] = 0.f;
-        if (PREPACKED && o_has) {
-            // each batch of four entries is in registers before its
-            // activations are read; the next batch loads meanwhile
-            const int ib = o_ib;
-            for (int i0 = o_ia + (lane >> 4); i0 < ib; i0 += 8) {
-                int col[4];
-                float d[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    col[u] = ocol[u];
-                    d[u] = odl[u];
-                }
-                if (i0 + 8 < ib) load_outliers(i0 + 8, ib);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    if (col[u] < kb || col[u] >= ke) continue;
-#pragma unroll
-                    for (int m = 0; m < MT; ++m)
-                        if (m < p.M) os[m] += d[u] * x_at(m, col[u]);
-                }
-            }
-        } else if (!PREPACKED && o_has) {
-            const int32_t* ro = p.off + (int64_t)row * (p.ncsr + 1);
-            int cc = kb / p.chunk_m;
-            const int cc_hi = (ke - 1) / p.chunk_m;
-            int bound = __ldg(ro + cc + 1);  // end of chunk cc
-            const int ib = __ldg(ro + cc_hi + 1);
-            for (int i = __ldg(ro + cc) + (lane >> 4); i < ib; i += 2) {
-                while (i >= bound) bound = __ldg(ro + (++cc) + 1);  // entries are chunk-ordered
-                const int col = cc * p.chunk_m + (int)__ldg(reinterpret_cast<const uint16_t*>(p.ccols) + i);
-                if (col < kb || col >= ke) continue;
-                const uint32_t sym = (__ldg(p.q + (int64_t)row * p.wpr + (col >> 3)) >> (4 * (col & 7))) & 15u;
-                const int grp = GROUPED ? ((col + p.goff) >> p.log2G) : 0;
-                const float wl = codebook_value<T, PREPACKED>(p.lut, (int64_t)row * p.ngroups + grp, sym);
-                const float d =
-                    f16_bits_to_f32(fp8_byte_to_f16_bits(__ldg(reinterpret_cast<const uint8_t*>(p.cvals) + i))) - wl;
-#pragma unroll
-                for (int m = 0; m < MT; ++m)
-                    if (m < p.M) os[m] += d * x_at(m, col);
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < MT; ++m) os[m] += __shfl_down_sync(0xFFFFFFFFu, os[m], 16);
-        if (lane < 16) {
-#pragma unroll
-            for (int m = 0; m < MT; ++m) part[warp][rl][m] = os[m];  // the MMA tile is added at publish
-        }
-        __syncwarp();
-    }
-
-    uint4 xnext[NT];
-#pragma unroll
-    for (int tt = 0; tt < NT; ++tt) xnext[tt] = c_begin < c_end ? lds_x8(tt, 0) : make_uint4(0u, 0u, 0u, 0u);
-
-    int st = 0;
-    for (int c = c_begin; c < c_end; ++c) {
-        cp_async_wait<S - 2>();  // this lane's copies of chunk c have landed
-        __syncwarp();            // ... and every lane's; the previous stage is free
-        issue(c + S - 1, st == 0 ? S - 1 : st - 1);
-        const uint32_t base = ring + (uint32_t)(st * R::kStageBytes);
-        st = st + 1 == S ? 0 : st + 1;
-        const uint4 w0 = lds128(base + g * 64 + 16 * t);
-        const uint4 w1 = lds128(base + (g + 8) * 64 + 16 * t);
-        LutPlanes P0, P1;
-        if (GROUPED) {
-            const int s = group_at(c * kChunk + 32 * t) - group_at(c * kChunk);
-            const uint32_t pb = base + R::kIdxBytes + s * 32;
-            planes_from_smem<T, PREPACKED>(pb + g * (NSLOT * 32), P0);
-            planes_from_smem<T, PREPACKED>(pb + (g + 8) * (NSLOT * 32), P1);
-        } else {
-            P0 = PR0;
-            P1 = PR1;
-        }
-        const uint32_t ra[4] = {w0.x, w0.y, w0.z, w0.w};
-        const uint32_t rb[4] = {w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-        for (int ws = 0; ws < 4; ++ws) {
-            uint4 xv[NT];
-#pragma unroll
-            for (int tt = 0; tt < NT; ++tt) {
-                xv[tt] = xnext[tt];
-                // next pair: this chunk's ws+1, or the next chunk's first
-                const int kn = (c - c_begin) * kChunk + (ws < 3 ? 8 * (ws + 1) : kChunk);
-                if (ws < 3 || c + 1 < c_end) xnext[tt] = lds_x8(tt, kn);
-            }
-            const uint32_t sa = ra[ws] & 0x77777777u;
-            const uint32_t ca = lop_and_or(mulhi(ra[ws], m31), 0x44444444u, 0x32103210u);
-            const uint32_t sb = rb[ws] & 0x77777777u;
-            const uint32_t cb2 = lop_and_or(mulhi(rb[ws], m31), 0x44444444u, 0x32103210u);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t a[4];
-                if (h == 0) {
-                    lookup4(P0, sa, ca, a[0], a[2]);
-                    lookup4(P1, sb, cb2, a[1], a[3]);
-                } else {
-                    lookup4(P0, mulhi(sa, m16), mulhi(ca, m16), a[0], a[2]);
-                    lookup4(P1, mulhi(sb, m16), mulhi(cb2, m16), a[1], a[3]);
-                }
-#pragma unroll
-                for (int tt = 0; tt < NT; ++tt) {
-                    const uint32_t b0 = h ? xv[tt].z : xv[tt].x;
-                    const uint32_t b1 = h ? xv[tt].w : xv[tt].y;
-                    Mma16816<T>::run(acc[tt], a, b0, b1);
-                }
-            }
-        }
-    }
-    // publish this warp's partial tile
-#pragma unroll
-    for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            part[warp][g][8 * tt + 2 * t + e] += acc[tt][e];
-            part[warp][g + 8][8 * tt + 2 * t + e] += acc[tt][2 + e];
-        }
-    __syncwarp();
-
-    const bool clustered = gridDim.y > 1;
-    if (clustered) cluster_sync_all();  // every rank's partial tiles are visible cluster-wide
-    const uint32_t rank = clustered ? cluster_ctarank() : 0u;
-    const uint32_t nranks = clustered ? cluster_nctarank() : 1u;
-    if (p.tp_world > 1) {
-        if (rank == 0) tp_allreduce_tile<T, MT>(p, part[warp], nranks, tile_row0, lane, gam);
-    } else {
-        // every rank finishes the tile rows rl with rl % nranks == rank; the
-        // sum over ranks is in rank order, so the result does not depend on
-        // which rank computes it.  s * B h is already in the tile.
-        for (int e = lane; e < kRowsPerTile * MT; e += 32) {
-            const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;  // rl == lane % 16
-            const int n = tile_row0 + rl;
-            if (n >= p.N || tk >= p.M || (uint32_t)rl % nranks != rank) continue;
-            const float s = cluster_sum(&part[warp][rl][tk], nranks) * gam;
-            reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s);
-        }
-    }
-    if (clustered) cluster_sync_all();  // keep every rank's tiles alive until all reads are done
-}
-
-constexpr int kStages = 3;  // measured: 3 >= 4 > 6 (more stages cost occupancy, not latency)
-
-template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM>
-int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream) {
-    auto kern = gemv_kernel<T, NT, NSLOT, PREPACKED, XVEC, XSMEM, kStages>;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)ctas, (unsigned)cs, 1);
-    cfg.blockDim = dim3(kWarps * 32, 1, 1);
-    const size_t smem = (size_t)p.x_bytes + (size_t)kWarps * kStages * Ring<NSLOT>::kStageBytes;
-    // the default limit covers static + dynamic shared memory up to 48 KB
-    constexpr size_t kStatic = sizeof(float) * kWarps * kRowsPerTile * 8 * NT;
-    if (smem + kStatic > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return check_cuda(e, "gemv_kernel smem attribute");
-    }
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = (unsigned)cs;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = cs > 1 ? 1 : 0;
-    return check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "gemv_kernel launch");
-}
 
 template <typename T, int NT, int NSLOT, bool PREPACKED>
 int dispatch_x(const GemvParams& p, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
     if (xsmem)
-        return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, true>(p, ctas, cs, stream)
-                    : launch_variant<T, NT, NSLOT, PREPACKED, false, true>(p, ctas, cs, stream);
-    return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, false>(p, ctas, cs, stream)
-                : launch_variant<T, NT, NSLOT, PREPACKED, false, false>(p, ctas, cs, stream);
+        return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, true, 0>(p, ctas, cs, stream)
+                    : launch_variant<T, NT, NSLOT, PREPACKED, false, true, 0>(p, ctas, cs, stream);
+    return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, false, 0>(p, ctas, cs, stream)
+                : launch_variant<T, NT, NSLOT, PREPACKED, false, false, 0>(p, ctas, cs, stream);
 }
 
 template <typename T, int NT, int NSLOT>
@@ -570,10 +55,6 @@ int dispatch_fmt(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int
     return prepacked ? dispatch_x<T, NT, NSLOT, true>(p, xvec, xsmem, ctas, cs, stream)
                      : dispatch_x<T, NT, NSLOT, false>(p, xvec, xsmem, ctas, cs, stream);
 }
-
-// codebook slots a 128-column chunk needs per row: 1 without grouping
-// (registers, no slot), 2 for groups of >= 128 columns, 4 for 32 and 64
-inline int codebook_slots(int G) { return G == 0 ? 0 : G >= kChunk ? 2 : 4; }
 
 template <typename T, int NT>
 int dispatch_slots(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs,
@@ -607,7 +88,7 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     GemvParams p;
     p.q = a.q; p.lut = a.lut; p.x = a.x; p.out = a.out;
     p.off = a.off; p.ccols = a.ccols; p.cvals = a.cvals;
-    p.loraB = a.loraB; p.lorah = a.lorah; p.gamma = a.gamma; p.scale = a.scale; p.r = a.r;
+    p.loraB = a.loraB; p.lorah = a.lorah; p.loraA = a.loraA; p.gamma = a.gamma; p.scale = a.scale; p.r = a.r;
     p.M = a.M; p.N = a.N; p.K = a.K; p.wpr = a.wpr; p.G = a.group_size; p.goff = a.group_offset;
     p.ngroups = a.ngroups; p.chunk_m = a.chunk_m; p.ncsr = a.ncsr;
     p.log2G = log2G;
@@ -629,6 +110,16 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
         p.tp_err = reinterpret_cast<uint32_t*>(mine + l.err);
     }
     const bool xvec = (a.K % 8 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
+    // h = A x in the kernel: r <= 16 rt
+    const int rt = a.loraA != nullptr && a.r > 0 ? (a.r <= 16 ? 1 : 2) : 0;
+    if (rt > 0) {
+        if (a.r > 32) return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: h = A x in the kernel needs r <= 32 (r=%d)", a.r);
+        if (!a.lut_prepacked)
+            return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: h = A x in the kernel needs the prepacked layout");
+        if (!xvec || (reinterpret_cast<uintptr_t>(a.loraA) & 15) != 0)
+            return fail(WLQ_ERR_ALIGNMENT, "wlq_gemv: h = A x in the kernel needs K %% 8 == 0 and 16-byte aligned "
+                        "x and lora_A");
+    }
 
     const int tiles = (a.N + kRowsPerTile - 1) / kRowsPerTile;
     const int ctas = (tiles + kWarps - 1) / kWarps;
@@ -642,10 +133,11 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     // stage the rank's activations in shared memory when 4 CTAs per SM still
     // fit beside the rings; larger slices are read through L1
     const int slots = codebook_slots(p.G);
-    const int ring_bytes = kWarps * kStages * (kRowsPerTile * 64 + kRowsPerTile * slots * 32);
+    const int ring_bytes = kWarps * kStages * ring_stage_bytes(slots, rt);
     const int64_t x_bytes = ((int64_t)a.M * p.x_stride * 2 + 127) / 128 * 128;
     const bool xsmem = x_bytes + ring_bytes <= 48 * 1024;
     p.x_bytes = xsmem ? (int)x_bytes : 0;
+    if (rt > 0) return launch_fold(p, rt, a.dtype == WLQ_DTYPE_BF16, xsmem, ctas, cs, stream);
     if (a.dtype == WLQ_DTYPE_BF16) return dispatch<__nv_bfloat16>(p, a.lut_prepacked, xvec, xsmem, ctas, cs, stream);
     return dispatch<__half>(p, a.lut_prepacked, xvec, xsmem, ctas, cs, stream);
 }

@@ -1,0 +1,47 @@
+// Instantiations of the decode GEMV that computes the DoRA low-rank input
+// h = A x itself (RT = 1 for r <= 16, 2 for r <= 32): the F.linear(x, A) and
+// .float() launches that precede every reference GEMV
+// (vllm_wlq/linear_method.py:962-963) folded into the one kernel.  Prepacked
+// codebooks and outliers and 16-byte aligned rows only, as the load path
+// always produces; kept in their own translation unit so the two halves of
+// the GEMV compile in parallel.
+#include "wlq_gemv_kernel.cuh"
+
+namespace wlq {
+namespace gemv {
+
+namespace {
+
+template <typename T, int NT, int NSLOT>
+int fold_x(const GemvParams& p, int rt, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+    if (rt == 1)
+        return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 1>(p, ctas, cs, stream)
+                     : launch_variant<T, NT, NSLOT, true, true, false, 1>(p, ctas, cs, stream);
+    return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 2>(p, ctas, cs, stream)
+                 : launch_variant<T, NT, NSLOT, true, true, false, 2>(p, ctas, cs, stream);
+}
+
+template <typename T, int NT>
+int fold_slots(const GemvParams& p, int rt, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+    switch (codebook_slots(p.G)) {
+        case 0: return fold_x<T, NT, 0>(p, rt, xsmem, ctas, cs, stream);
+        case 2: return fold_x<T, NT, 2>(p, rt, xsmem, ctas, cs, stream);
+        default: return fold_x<T, NT, 4>(p, rt, xsmem, ctas, cs, stream);
+    }
+}
+
+template <typename T>
+int fold_tokens(const GemvParams& p, int rt, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+    return p.M <= 8 ? fold_slots<T, 1>(p, rt, xsmem, ctas, cs, stream)
+                    : fold_slots<T, 2>(p, rt, xsmem, ctas, cs, stream);
+}
+
+}  // namespace
+
+int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+    return bf16 ? fold_tokens<__nv_bfloat16>(p, rt, xsmem, ctas, cs, stream)
+                : fold_tokens<__half>(p, rt, xsmem, ctas, cs, stream);
+}
+
+}  // namespace gemv
+}  // namespace wlq

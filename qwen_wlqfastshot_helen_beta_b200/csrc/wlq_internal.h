@@ -24,6 +24,7 @@ struct LinearArgs {
     const void* cvals;       // [nnz] e5m2 bytes, or float32 corrections when prepacked; or null
     const uint16_t* loraB;   // fp16 [N, r] or null
     const float* lorah;      // fp32 [M, r] or null
+    const uint16_t* loraA = nullptr;  // act dtype [r, K]: the GEMV computes h = A x (lorah null)
     const uint16_t* gamma;   // fp16 [N] or null
     float scale;
     int r;                   // 0 when the DoRA term is off

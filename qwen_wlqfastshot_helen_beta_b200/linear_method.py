@@ -477,18 +477,25 @@ class WLQLinearMethod(LinearMethodBase):
                 cols, vals = layer.cols_packed, layer.delta_packed
         else:
             lut, fmt = layer.lut_c, 0
-        lora_h = None
+        lora_h = lora_A = None
         if has_dora and layer.lora_A_f16 is not None:
-            lora_h = F.linear(x2, self._lora_A(layer, x2.dtype)).float()
+            A = self._lora_A(layer, x2.dtype)
+            # decode: the GEMV computes h = A x itself (one launch instead of
+            # F.linear + .float() + GEMV) when its layout allows
+            if M <= 16 and fmt == 1 and 0 < lora_B.shape[1] <= 32 and layer.K % 8 == 0 and \
+                    x2.data_ptr() % 16 == 0 and A.data_ptr() % 16 == 0:
+                lora_A = A
+            else:
+                lora_h = F.linear(x2, A).float()
         if M == 1:
             torch.ops.wlq_fastShot.gemv(layer.q_packed_aligned, lut, x2.squeeze(0), out.squeeze(0), layer.N,
                                         layer.K, bits, layer.chunk_offsets, cols, vals,
                                         lora_B, None if lora_h is None else lora_h.squeeze(0), gamma, scale, G, goff,
-                                        fmt)
+                                        fmt, lora_A)
         else:
             torch.ops.wlq_fastShot.gemm(x2, layer.q_packed_aligned, lut, out, layer.N, layer.K, bits,
                                         layer.words_per_row, layer.chunk_offsets, cols, vals, lora_h, lora_B,
-                                        gamma, scale, G, goff, fmt)
+                                        gamma, scale, G, goff, fmt, lora_A)
         if out.dtype != orig_dtype:
             out = out.to(orig_dtype)
         if bias is not None:

@@ -49,9 +49,12 @@ class SyntheticLayer:
     cols_packed: Optional[torch.Tensor] = None
     delta_packed: Optional[torch.Tensor] = None
     packed_dtype: Optional[torch.dtype] = None
+    lora_A_act: Optional[torch.Tensor] = None   # A in packed_dtype, for the GEMV that computes h = A x
 
     def prepack(self, act_dtype: torch.dtype) -> "SyntheticLayer":
         self.lut_packed = _C.prepack_lut(self.lut_c.contiguous(), act_dtype)
+        if self.lora_A is not None:
+            self.lora_A_act = self.lora_A.to(act_dtype).contiguous()
         if self.chunk_cols is not None and self.q_packed.is_cuda:
             self.cols_packed, self.delta_packed = _C.prepack_outliers(
                 self.q_packed, self.lut_c, self.chunk_offsets, self.chunk_cols, self.chunk_vals, self.N, self.K, 4,
@@ -72,13 +75,14 @@ class SyntheticLayer:
 
     def algorithmic_bytes(self, M: int) -> int:
         """HBM bytes one forward must move: indices, codebooks, outlier CSR,
-        DoRA tensors (B, gamma, and h = A x as M*r fp32), x and out (2 B)."""
+        DoRA tensors (A and B as 2-byte [r, K] and [N, r], gamma), x and out
+        (2 B); h = A x is an intermediate of the forward."""
         ncsr = (self.K + 511) // 512
         b = self.N * self.words_per_row * 4 + self.lut_c.numel() * 2
         if self.chunk_cols is not None:
             b += self.N * (ncsr + 1) * 4 + 3 * self.nnz
         if self.lora_B is not None:
-            b += self.N * self.r * 2 + self.N * 2 + M * self.r * 4
+            b += self.N * self.r * 2 + self.N * 2 + self.r * self.K * 2
         b += M * self.K * 2 + M * self.N * 2
         return b
 
@@ -202,6 +206,18 @@ def forward(layer: SyntheticLayer, x: torch.Tensor, out: Optional[torch.Tensor] 
     _C.gemm_forward(x, layer.q_packed, lut, out, layer.N, layer.K, 4, layer.words_per_row,
                     layer.chunk_offsets, cols, vals, h, layer.lora_B, layer.dora_gamma,
                     layer.lora_scale, layer.group_size, layer.group_offset, fmt)
+    return out
+
+
+def forward_fold(layer: SyntheticLayer, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode forward (M <= 16) with h = A x computed inside the GEMV
+    (prepacked layer, x in its packed dtype)."""
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, layer.N), dtype=x.dtype, device=x.device)
+    lut, cols, vals, fmt = layer.operands_for(x.dtype)
+    _C.gemv_lora_a(layer.q_packed, lut, x, out, layer.N, layer.K, 4, layer.chunk_offsets, cols, vals, layer.lora_B,
+                   layer.lora_A_act, layer.dora_gamma, layer.lora_scale, layer.group_size, layer.group_offset, fmt)
     return out
 
 

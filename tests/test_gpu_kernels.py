@@ -91,6 +91,62 @@ def test_gemv_matches_oracle(case, dtype):
         assert torch.equal(ys[0], ys[1])  # same arithmetic either way
 
 
+FOLD_CASES = [
+    # N, K, G, goff, r
+    (64, 1024, 0, 0, 16),      # per-row codebooks, K split over a 3-CTA cluster (ranks of 3, 3, 2 chunks)
+    (100, 4096, 128, 0, 16),   # per-group codebooks, 8-CTA cluster
+    (48, 448, 128, 64, 8),     # shard starting mid-group, rank below one MMA tile
+    (300, 1024, 32, 0, 24),    # 32-wide groups, rank in two MMA tiles
+    (64, 18944, 128, 0, 32),   # activations too large to stage, read through L1
+    (1200, 512, 128, 0, 16),   # many row tiles, no cluster
+]
+
+
+@pytest.mark.parametrize("case", FOLD_CASES, ids=lambda c: f"N{c[0]}K{c[1]}G{c[2]}o{c[3]}r{c[4]}")
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_gemv_lora_a_matches_oracle(case, dtype):
+    """wlq_gemv_lora_a (h = A x computed inside the GEMV) against the oracle
+    with the reference's h = fp16(A x), and against the GEMV given that h."""
+    N, K, G, goff, r = case
+    rng = np.random.default_rng(N + K + r)
+    L = make_np_layer(rng, N, K, G, goff, density=0.02, r=r)
+    T = dev_layer(L)
+    lut = C().prepack_lut(T["lut"], dtype)
+    cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], L.N, L.K, 4, dtype, L.G,
+                                      L.goff)
+    A = T["A"].to(dtype).contiguous()
+    for M in (1, 2, 5, 8, 9, 16):
+        x, h = inputs(rng, L, M, dtype)
+        ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+        y = torch.full((M, N), float("nan"), dtype=dtype, device="cuda")
+        C().gemv_lora_a(T["q"], lut, x, y, N, K, 4, T["off"], cols, vals, T["B"], A, T["gamma"], L.scale, L.G,
+                        L.goff)
+        torch.cuda.synchronize()
+        assert torch.isfinite(y).all(), M
+        e = rel_err(y.float().cpu().numpy(), ref)
+        assert e <= TOL[dtype], (M, e)
+        y_h = run_ours(L, T, x, h, gemv=(M == 1), fmt=1)
+        assert rel_err(y.float().cpu().numpy(), y_h.float().cpu().numpy()) <= 1e-2, M
+
+
+def test_gemv_lora_a_rejects():
+    """The in-kernel h needs the prepacked layout, r <= 32 and 16-byte rows."""
+    rng = np.random.default_rng(3)
+    L = make_np_layer(rng, 32, 256, 0, 0, r=48)
+    T = dev_layer(L)
+    x = torch.randn((2, 256), device="cuda", dtype=torch.float16)
+    y = torch.empty((2, 32), device="cuda", dtype=torch.float16)
+    lut = C().prepack_lut(T["lut"], torch.float16)
+    cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], 32, 256, 4, torch.float16)
+    with pytest.raises(RuntimeError, match="r <= 32"):
+        C().gemv_lora_a(T["q"], lut, x, y, 32, 256, 4, T["off"], cols, vals, T["B"], T["A"], T["gamma"], 1.0)
+    L = make_np_layer(rng, 32, 256, 0, 0, r=16)
+    T = dev_layer(L)
+    with pytest.raises(RuntimeError, match="prepacked"):
+        C().gemv_lora_a(T["q"], T["lut"], x, y, 32, 256, 4, T["off"], T["cols"], T["vals"], T["B"], T["A"],
+                        T["gamma"], 1.0, lut_format=0)
+
+
 def test_gemv_outlier_edges():
     """Outliers at the first and last column, in a ragged last chunk, a row
     made only of outliers, and rows without any."""

@@ -1,7 +1,8 @@
 """Fused row-parallel all-reduce (wlq_gemv_allreduce) on 2 GPUs: each rank's
 K shard through the GEMV with the sum over ranks done in the kernel over
 NVLink peer memory, against the ranks' own outputs summed after an NCCL
-all-gather.  Eager calls and CUDA-graph replays (the per-tile epochs advance
+all-gather.  Eager calls (h given, or h = A x of the rank's columns of A
+computed in the kernel) and CUDA-graph replays (the per-tile epochs advance
 on the device), several token counts.  Skipped with fewer than 2 GPUs."""
 import os
 import socket
@@ -44,7 +45,12 @@ def _rank_main(rank, port, results):
         gen = torch.Generator(device=dev)
         gen.manual_seed(9 + rank)
 
-        def fused(x, h, out):
+        def fused(x, h, out, in_kernel_h=False):
+            if in_kernel_h:  # this rank's columns of A, h = A x computed in the kernel
+                _C.gemv_allreduce(comm, x, L.q_packed, lut, out, N, Kp, 4, L.words_per_row, L.chunk_offsets, cols,
+                                  vals, None, L.lora_B, L.dora_gamma, L.lora_scale, L.group_size, L.group_offset,
+                                  fmt, lora_A=L.lora_A_act)
+                return
             _C.gemv_allreduce(comm, x, L.q_packed, lut, out, N, Kp, 4, L.words_per_row, L.chunk_offsets, cols,
                               vals, h, L.lora_B, L.dora_gamma, L.lora_scale, L.group_size, L.group_offset, fmt)
 
@@ -56,11 +62,11 @@ def _rank_main(rank, port, results):
             errs.append(float((y.float() - ref).abs().max() / ref.abs().max()))
 
         for M in (1, 5, 16):
-            for _ in range(3):  # repeated calls: epochs and slot parity advance
+            for i in range(4):  # repeated calls: epochs and slot parity advance
                 x = torch.randn((M, Kp), generator=gen, device=dev).to(torch.bfloat16)
                 h = S.lora_h(L, x)
                 y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-                fused(x, h, y)
+                fused(x, h, y, in_kernel_h=i % 2 == 1)
                 check(x, h, y)
         # the same inside a CUDA graph, replayed with new inputs
         M = 8
