@@ -33,6 +33,10 @@
 // its tile (the arithmetic of csrc/gemv_kernel.cu:262-288): two lanes per row
 // walk the row's chunk-CSR entries, accumulate in registers and combine with
 // one shuffle.
+#include <mutex>
+#include <utility>
+#include <vector>
+
 #include "wlq_gemv_kernel.cuh"
 
 namespace wlq {
@@ -42,37 +46,79 @@ using namespace gemv;
 namespace {
 
 template <typename T, int NT, int NSLOT, bool PREPACKED>
-int dispatch_x(const GemvParams& p, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+int dispatch_x(const GemvParams& p, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream, int* fit) {
     if (xsmem)
-        return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, true, 0>(p, ctas, cs, stream)
-                    : launch_variant<T, NT, NSLOT, PREPACKED, false, true, 0>(p, ctas, cs, stream);
-    return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, false, 0>(p, ctas, cs, stream)
-                : launch_variant<T, NT, NSLOT, PREPACKED, false, false, 0>(p, ctas, cs, stream);
+        return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, true, 0>(p, ctas, cs, stream, fit)
+                    : launch_variant<T, NT, NSLOT, PREPACKED, false, true, 0>(p, ctas, cs, stream, fit);
+    return xvec ? launch_variant<T, NT, NSLOT, PREPACKED, true, false, 0>(p, ctas, cs, stream, fit)
+                : launch_variant<T, NT, NSLOT, PREPACKED, false, false, 0>(p, ctas, cs, stream, fit);
 }
 
 template <typename T, int NT, int NSLOT>
-int dispatch_fmt(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
-    return prepacked ? dispatch_x<T, NT, NSLOT, true>(p, xvec, xsmem, ctas, cs, stream)
-                     : dispatch_x<T, NT, NSLOT, false>(p, xvec, xsmem, ctas, cs, stream);
+int dispatch_fmt(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream,
+                 int* fit) {
+    return prepacked ? dispatch_x<T, NT, NSLOT, true>(p, xvec, xsmem, ctas, cs, stream, fit)
+                     : dispatch_x<T, NT, NSLOT, false>(p, xvec, xsmem, ctas, cs, stream, fit);
 }
 
 template <typename T, int NT>
 int dispatch_slots(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, int* fit) {
     switch (codebook_slots(p.G)) {
-        case 0: return dispatch_fmt<T, NT, 0>(p, prepacked, xvec, xsmem, ctas, cs, stream);
-        case 2: return dispatch_fmt<T, NT, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream);
-        default: return dispatch_fmt<T, NT, 4>(p, prepacked, xvec, xsmem, ctas, cs, stream);
+        case 0: return dispatch_fmt<T, NT, 0>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit);
+        case 2: return dispatch_fmt<T, NT, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit);
+        default: return dispatch_fmt<T, NT, 4>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit);
     }
 }
 
 template <typename T>
-int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream) {
-    return p.M <= 8 ? dispatch_slots<T, 1>(p, prepacked, xvec, xsmem, ctas, cs, stream)
-                    : dispatch_slots<T, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream);
+int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream,
+             int* fit) {
+    return p.M <= 8 ? dispatch_slots<T, 1>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit)
+                    : dispatch_slots<T, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit);
 }
 
+// One launch shape: K split over cs CTAs; activations staged in shared
+// memory or read through L1.
+struct Plan {
+    int cs;
+    bool xsmem, stages2;
+};
+
+struct FitKey {
+    const void* kern;
+    unsigned cx, cy;
+    size_t smem;
+    int dev;
+};
+
 }  // namespace
+
+namespace gemv {
+
+int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit) {
+    static std::mutex mu;
+    static std::vector<std::pair<FitKey, int>> cache;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return check_cuda(e, "cudaGetDevice");
+    const FitKey key{kern, cfg.attrs[0].val.clusterDim.x, cfg.attrs[0].val.clusterDim.y, cfg.dynamicSmemBytes, dev};
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& kv : cache)
+        if (kv.first.kern == key.kern && kv.first.cx == key.cx && kv.first.cy == key.cy &&
+            kv.first.smem == key.smem && kv.first.dev == key.dev) {
+            *fit = kv.second;
+            return WLQ_OK;
+        }
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess) return check_cuda(e, "cudaOccupancyMaxActiveClusters");
+    cache.emplace_back(key, n);
+    *fit = n;
+    return WLQ_OK;
+}
+
+}  // namespace gemv
 
 int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     if (a.M == 0 || a.N == 0) return WLQ_OK;
@@ -120,26 +166,53 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
             return fail(WLQ_ERR_ALIGNMENT, "wlq_gemv: h = A x in the kernel needs K %% 8 == 0 and 16-byte aligned "
                         "x and lora_A");
     }
-
+    const bool bf16 = a.dtype == WLQ_DTYPE_BF16;
     const int tiles = (a.N + kRowsPerTile - 1) / kRowsPerTile;
     const int ctas = (tiles + kWarps - 1) / kWarps;
-    // Split K over a cluster until about 4 CTAs (16 warps) per SM are in
-    // flight, keeping at least 2 chunks per rank.
-    const int sms = device_sm_count();
-    int cs = 1;
-    while (cs < 8 && (int64_t)ctas * cs < 4LL * sms && p.kchunks >= 2 * (cs + 1)) ++cs;
-    p.chunks_per_rank = (p.kchunks + cs - 1) / cs;
-    p.x_stride = p.chunks_per_rank * kChunk + 8;
-    // stage the rank's activations in shared memory when 4 CTAs per SM still
-    // fit beside the rings; larger slices are read through L1
     const int slots = codebook_slots(p.G);
     const int ring_bytes = kWarps * kStages * ring_stage_bytes(slots, rt);
-    const int64_t x_bytes = ((int64_t)a.M * p.x_stride * 2 + 127) / 128 * 128;
-    const bool xsmem = x_bytes + ring_bytes <= 48 * 1024;
-    p.x_bytes = xsmem ? (int)x_bytes : 0;
-    if (rt > 0) return launch_fold(p, rt, a.dtype == WLQ_DTYPE_BF16, xsmem, ctas, cs, stream);
-    if (a.dtype == WLQ_DTYPE_BF16) return dispatch<__nv_bfloat16>(p, a.lut_prepacked, xvec, xsmem, ctas, cs, stream);
-    return dispatch<__half>(p, a.lut_prepacked, xvec, xsmem, ctas, cs, stream);
+
+    auto configure = [&](int cs) {
+        Plan pl;
+        pl.cs = cs;
+        p.chunks_per_rank = (p.kchunks + cs - 1) / cs;
+        p.x_stride = p.chunks_per_rank * kChunk + 8;
+        // stage the rank's activations in shared memory when 4 CTAs per SM
+        // still fit beside the rings; larger slices are read through L1.
+        // Computing h (larger stages) for 9..16 tokens, a 2-stage ring when
+        // that lets the activations be staged.
+        const int64_t x_bytes = ((int64_t)a.M * p.x_stride * 2 + 127) / 128 * 128;
+        pl.xsmem = x_bytes + ring_bytes <= 48 * 1024;
+        pl.stages2 = rt > 0 && a.M > 8 && !pl.xsmem && x_bytes + ring_bytes / kStages * 2 <= 48 * 1024;
+        pl.xsmem = pl.xsmem || pl.stages2;
+        p.x_bytes = pl.xsmem ? (int)x_bytes : 0;
+        return pl;
+    };
+    auto run = [&](const Plan& pl, int* fit) {
+        if (rt > 0) return launch_fold(p, rt, bf16, pl.xsmem, pl.stages2, ctas, pl.cs, stream, fit);
+        return bf16 ? dispatch<__nv_bfloat16>(p, a.lut_prepacked, xvec, pl.xsmem, ctas, pl.cs, stream, fit)
+                    : dispatch<__half>(p, a.lut_prepacked, xvec, pl.xsmem, ctas, pl.cs, stream, fit);
+    };
+
+    // Split K over a cluster until about 4 CTAs (16 warps) per SM are in
+    // flight, keeping at least 2 chunks per rank; then take the largest split
+    // (down to none) whose clusters the device holds in one wave.
+    const int sms = device_sm_count();
+    int cs_max = 1;
+    while (cs_max < 8 && (int64_t)ctas * cs_max < 4LL * sms && p.kchunks >= 2 * (cs_max + 1)) ++cs_max;
+    Plan pl = configure(1);
+    for (int cs = cs_max; cs > 1; --cs) {
+        const Plan c = configure(cs);
+        int fit = 0;
+        const int rc = run(c, &fit);
+        if (rc) return rc;
+        if (ctas <= fit) {
+            pl = c;
+            break;
+        }
+    }
+    configure(pl.cs);
+    return run(pl, nullptr);
 }
 
 }  // namespace wlq

@@ -13,34 +13,43 @@ namespace gemv {
 namespace {
 
 template <typename T, int NT, int NSLOT>
-int fold_x(const GemvParams& p, int rt, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+int fold_x(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int cs, cudaStream_t stream,
+           int* fit) {
+    if constexpr (NT == 2) {
+        if (stages2 && xsmem)  // 16 tokens staged beside a 2-stage ring
+            return rt == 1 ? launch_variant<T, NT, NSLOT, true, true, true, 1, 2>(p, ctas, cs, stream, fit)
+                           : launch_variant<T, NT, NSLOT, true, true, true, 2, 2>(p, ctas, cs, stream, fit);
+    }
     if (rt == 1)
-        return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 1>(p, ctas, cs, stream)
-                     : launch_variant<T, NT, NSLOT, true, true, false, 1>(p, ctas, cs, stream);
-    return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 2>(p, ctas, cs, stream)
-                 : launch_variant<T, NT, NSLOT, true, true, false, 2>(p, ctas, cs, stream);
+        return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 1>(p, ctas, cs, stream, fit)
+                     : launch_variant<T, NT, NSLOT, true, true, false, 1>(p, ctas, cs, stream, fit);
+    return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 2>(p, ctas, cs, stream, fit)
+                 : launch_variant<T, NT, NSLOT, true, true, false, 2>(p, ctas, cs, stream, fit);
 }
 
 template <typename T, int NT>
-int fold_slots(const GemvParams& p, int rt, bool xsmem, int ctas, int cs, cudaStream_t stream) {
+int fold_slots(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int cs, cudaStream_t stream,
+               int* fit) {
     switch (codebook_slots(p.G)) {
-        case 0: return fold_x<T, NT, 0>(p, rt, xsmem, ctas, cs, stream);
-        case 2: return fold_x<T, NT, 2>(p, rt, xsmem, ctas, cs, stream);
-        default: return fold_x<T, NT, 4>(p, rt, xsmem, ctas, cs, stream);
+        case 0: return fold_x<T, NT, 0>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
+        case 2: return fold_x<T, NT, 2>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
+        default: return fold_x<T, NT, 4>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
     }
 }
 
 template <typename T>
-int fold_tokens(const GemvParams& p, int rt, bool xsmem, int ctas, int cs, cudaStream_t stream) {
-    return p.M <= 8 ? fold_slots<T, 1>(p, rt, xsmem, ctas, cs, stream)
-                    : fold_slots<T, 2>(p, rt, xsmem, ctas, cs, stream);
+int fold_tokens(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int cs, cudaStream_t stream,
+                int* fit) {
+    return p.M <= 8 ? fold_slots<T, 1>(p, rt, xsmem, false, ctas, cs, stream, fit)
+                    : fold_slots<T, 2>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
 }
 
 }  // namespace
 
-int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, int ctas, int cs, cudaStream_t stream) {
-    return bf16 ? fold_tokens<__nv_bfloat16>(p, rt, xsmem, ctas, cs, stream)
-                : fold_tokens<__half>(p, rt, xsmem, ctas, cs, stream);
+int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, bool stages2, int ctas, int cs,
+                cudaStream_t stream, int* fit) {
+    return bf16 ? fold_tokens<__nv_bfloat16>(p, rt, xsmem, stages2, ctas, cs, stream, fit)
+                : fold_tokens<__half>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
 }
 
 }  // namespace gemv

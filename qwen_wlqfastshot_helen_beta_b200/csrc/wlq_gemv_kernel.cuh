@@ -554,11 +554,13 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
                     hmine[(16 * rt + g + 8) * MT + 8 * tt + 2 * t + e] = hacc[rt][tt][2 + e];
                 }
         __syncthreads();
+        auto warp_part = [&](int w) {
+            return reinterpret_cast<const float*>(smem + p.x_bytes + w * S * R::kStageBytes);
+        };
         auto hsum = [&](int k, int tok) -> float {  // s * h[k][tok] over the CTA's K range
             float v = 0.f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w)
-                v += reinterpret_cast<const float*>(smem + p.x_bytes + w * S * R::kStageBytes)[k * MT + tok];
+            for (int w = 0; w < kWarps; ++w) v += warp_part(w)[k * MT + tok];
             return p.scale * v;
         };
         auto pack = [](float lo, float hi) -> uint32_t {
@@ -593,7 +595,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
     const uint32_t rank = clustered ? cluster_ctarank() : 0u;
     const uint32_t nranks = clustered ? cluster_nctarank() : 1u;
     if (p.tp_world > 1) {
-        if (rank == 0) tp_allreduce_tile<T, MT>(p, part[warp], nranks, tile_row0, lane, gam);
+        // tiles past N (the grid's last CTA) have no epochs or slots
+        if (rank == 0 && tile_row0 < p.N) tp_allreduce_tile<T, MT>(p, part[warp], nranks, tile_row0, lane, gam);
     } else {
         // every rank finishes the tile rows rl with rl % nranks == rank; the
         // sum over ranks is in rank order, so the result does not depend on
@@ -618,13 +621,19 @@ inline int codebook_slots(int G) { return G == 0 ? 0 : G >= kChunk ? 2 : 4; }
 // bytes of one warp's ring stage (host side of Ring<NSLOT, RT>)
 inline int ring_stage_bytes(int slots, int rt) { return kRowsPerTile * 64 + kRowsPerTile * slots * 32 + rt * 16 * 64; }
 
-template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int RT>
-int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream) {
-    auto kern = gemv_kernel<T, NT, NSLOT, PREPACKED, XVEC, XSMEM, kStages, RT>;
+// Clusters of the launch shape `cfg` that the device holds at once (cached
+// per kernel, shape and shared memory size).
+int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit);
+
+// Launches one variant; with `fit` set, reports instead how many of its
+// clusters the device holds at once (INT_MAX when it runs without clusters).
+template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int RT, int STAGES = kStages>
+int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, int* fit = nullptr) {
+    auto kern = gemv_kernel<T, NT, NSLOT, PREPACKED, XVEC, XSMEM, STAGES, RT>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas, (unsigned)cs, 1);
     cfg.blockDim = dim3(kWarps * 32, 1, 1);
-    const size_t smem = (size_t)p.x_bytes + (size_t)kWarps * kStages * Ring<NSLOT, RT>::kStageBytes;
+    const size_t smem = (size_t)p.x_bytes + (size_t)kWarps * STAGES * Ring<NSLOT, RT>::kStageBytes;
     // the default limit covers static + dynamic shared memory up to 48 KB
     constexpr size_t kStatic = sizeof(float) * kWarps * kRowsPerTile * 8 * NT;
     if (smem + kStatic > 48 * 1024) {
@@ -633,20 +642,30 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream) {
     }
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[1];  // clusters split K: cs CTAs along y
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = (unsigned)cs;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = cs > 1 ? 1 : 0;
+    if (fit) {
+        if (cfg.numAttrs == 0) {
+            *fit = 0x7FFFFFFF;
+            return WLQ_OK;
+        }
+        return clusters_that_fit(reinterpret_cast<const void*>(kern), cfg, fit);
+    }
     return check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "gemv_kernel launch");
 }
 
 // Launches the kernel that computes h = A x itself (p.loraA, r <= 16 rt,
 // rt = 1 or 2; prepacked codebooks and outliers, 16-byte aligned rows).
 // Defined in wlq_gemv_fold.cu.
-int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, int ctas, int cs, cudaStream_t stream);
+// stages2: a 2-stage ring, which lets the activations of 16 tokens be staged
+// beside the larger stages of this kernel.
+int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, bool stages2, int ctas, int cs,
+                cudaStream_t stream, int* fit = nullptr);
 
 }  // namespace gemv
 }  // namespace wlq

@@ -99,6 +99,8 @@ FOLD_CASES = [
     (300, 1024, 32, 0, 24),    # 32-wide groups, rank in two MMA tiles
     (64, 18944, 128, 0, 32),   # activations too large to stage, read through L1
     (1200, 512, 128, 0, 16),   # many row tiles, no cluster
+    (4100, 384, 128, 0, 16),   # no K split, ragged last CTA
+    (18944, 1024, 128, 0, 32), # no K split, rank in two MMA tiles
 ]
 
 
@@ -264,6 +266,15 @@ def test_full_size_shapes(name):
         # the kernel multiplies bf16-rounded codebook values; compare against both
         e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
         assert e <= 2e-2, (name, M, e)
+    # the GEMV computing h = A x itself (the decode path apply() takes), every token count
+    L.prepack(torch.bfloat16)
+    for M in range(1, 17):
+        x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+        h = S.lora_h(L, x)
+        y = S.forward_fold(L, x)
+        ref = (x.float() @ Wf.t() + L.lora_scale * (h @ L.lora_B.float().t())) * L.dora_gamma.float()
+        e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
+        assert e <= 2e-2, (name, M, "h in the kernel", e)
     del W, Wf
 
 
