@@ -155,11 +155,33 @@ def gemv_forward(q_packed, lut_c, x, out, N, K, bits, chunk_offsets=None, chunk_
     check(rc, "wlq_gemv")
 
 
+_SM_COUNT = {}
+
+
+def folds_h(M, N, K, r, lut_format, x) -> bool:
+    """Whether gemv_lora_a takes this call (the GEMV computing h = A x): up
+    to 16 tokens with r <= 32, or 17..32 tokens with r <= 16 when the
+    tensor-core GEMM's 128-row tiles would not fill the device (the rule
+    wlq_gemm applies, csrc/wlq_abi.cu gemv_preferred); prepacked layout and
+    16-byte aligned rows either way."""
+    if not (0 < r <= 32 and lut_format == WLQ_LUT_PREPACKED and K % 8 == 0 and x.data_ptr() % 16 == 0):
+        return False
+    if M <= 16:
+        return True
+    if M > 32 or r > 16:
+        return False
+    dev = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    if dev not in _SM_COUNT:
+        _SM_COUNT[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
+    return (N + 127) // 128 < _SM_COUNT[dev]
+
+
 def gemv_lora_a(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_A,
                 dora_gamma, lora_scale=1.0, lut_group_size=0, lut_group_offset=0, lut_format=WLQ_LUT_PREPACKED):
-    """Decode GEMV (M <= 16) that computes the DoRA input h = lora_A x itself
-    (lora_A [r, K] in x's dtype, r <= 32; prepacked layout): one launch in
-    place of F.linear + .float() + GEMV (vllm_wlq/linear_method.py:962-999)."""
+    """Decode GEMV (M <= 32) that computes the DoRA input h = lora_A x itself
+    (lora_A [r, K] in x's dtype, r <= 32, r <= 16 above 16 tokens; prepacked
+    layout): one launch in place of F.linear + .float() + GEMV
+    (vllm_wlq/linear_method.py:962-999)."""
     N, K, bits = int(N), int(K), int(bits)
     offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
     lb, la, gm = _opt(lora_B), _opt(lora_A), _opt(dora_gamma)

@@ -79,11 +79,11 @@ def _register_ops():
     ) -> None:
         if lora_A is not None and lora_H is None:
             M = X.numel() // int(K)
-            if M <= 16:  # h = A x inside the GEMV: one launch
+            if _C.folds_h(M, int(N), int(K), int(lora_A.shape[0]), lut_format, X):  # h = A x inside the GEMV
                 _C.gemv_lora_a(q_packed, lut_c, X, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
                                lora_A, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
                 return
-            # prefill: h = A x as one library GEMM, as the reference computes it
+            # otherwise h = A x as one library GEMM, as the reference computes it
             lora_H = torch.nn.functional.linear(X.reshape(M, int(K)), lora_A).float()
         _C.gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets, chunk_cols,
                         chunk_vals, lora_H, lora_B, dora_gamma, lora_scale, lut_group_size, lut_group_offset,

@@ -117,6 +117,14 @@ int build_args(const char* fn, const void* x, const int32_t* q, const void* lut,
 }
 }  // namespace
 
+bool gemv_preferred(int M, int N, int K, bool prepacked, const void* x) {
+    if (M <= 16) return true;
+    // 17..32 tokens: the GEMV (weights streamed once, one launch) unless the
+    // tensor-core GEMM's 128-row tiles fill the device
+    const bool gemv_ok = M <= 32 && prepacked && K % 8 == 0 && aligned(x, 16);
+    return gemv_ok && (N + 127) / 128 < device_sm_count();
+}
+
 int device_sm_count() {
     int dev = 0;
     if (current_device(&dev) != WLQ_OK) return 148;
@@ -160,7 +168,7 @@ int wlq_gemv_lora_a(const int32_t* q_packed, const void* lut_c, const void* x, v
                         nullptr, lora_A, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size,
                         lut_group_offset, lut_format, act_dtype, a);
     if (rc) return rc;
-    if (M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_lora_a: M must be 1..16 (got %d)", M);
+    if (M > 32) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_lora_a: M must be 1..32 (got %d)", M);
     if (M == 0 || N == 0) return WLQ_OK;
     if ((rc = require_sm100())) return rc;
     return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
@@ -178,7 +186,7 @@ int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* ou
     if (rc) return rc;
     if (M == 0 || N == 0) return WLQ_OK;
     if ((rc = require_sm100())) return rc;
-    if (M <= 16) return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
+    if (gemv_preferred(M, N, K, a.lut_prepacked, X)) return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
     return launch_gemm(a, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -71,9 +71,26 @@ int dispatch_slots(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, i
     }
 }
 
+// 17..32 tokens (four 8-token MMA tiles): prepacked layout, 16-byte rows
+template <typename T>
+int dispatch32(const GemvParams& p, bool xsmem, int ctas, int cs, cudaStream_t stream, int* fit) {
+    switch (codebook_slots(p.G)) {
+        case 0:
+            return xsmem ? launch_variant<T, 4, 0, true, true, true, 0>(p, ctas, cs, stream, fit)
+                         : launch_variant<T, 4, 0, true, true, false, 0>(p, ctas, cs, stream, fit);
+        case 2:
+            return xsmem ? launch_variant<T, 4, 2, true, true, true, 0>(p, ctas, cs, stream, fit)
+                         : launch_variant<T, 4, 2, true, true, false, 0>(p, ctas, cs, stream, fit);
+        default:
+            return xsmem ? launch_variant<T, 4, 4, true, true, true, 0>(p, ctas, cs, stream, fit)
+                         : launch_variant<T, 4, 4, true, true, false, 0>(p, ctas, cs, stream, fit);
+    }
+}
+
 template <typename T>
 int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream,
              int* fit) {
+    if (p.M > 16) return dispatch32<T>(p, xsmem, ctas, cs, stream, fit);
     return p.M <= 8 ? dispatch_slots<T, 1>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit)
                     : dispatch_slots<T, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit);
 }
@@ -122,7 +139,10 @@ int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit)
 
 int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     if (a.M == 0 || a.N == 0) return WLQ_OK;
-    if (a.M > 16) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: M must be <= 16, got %d", a.M);
+    if (a.M > kMaxGemvM) return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: M must be <= %d, got %d", kMaxGemvM, a.M);
+    if (a.M > 16 && (!a.lut_prepacked || a.K % 8 != 0 || (reinterpret_cast<uintptr_t>(a.x) & 15) != 0))
+        return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: 17..%d tokens need the prepacked layout and 16-byte aligned rows",
+                    kMaxGemvM);
     int log2G = 0;
     if (a.group_size > 0) {
         while ((1 << log2G) < a.group_size) ++log2G;
@@ -160,6 +180,8 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     const int rt = a.loraA != nullptr && a.r > 0 ? (a.r <= 16 ? 1 : 2) : 0;
     if (rt > 0) {
         if (a.r > 32) return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: h = A x in the kernel needs r <= 32 (r=%d)", a.r);
+        if (a.M > 16 && a.r > 16)
+            return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: h = A x in the kernel for more than 16 tokens needs r <= 16");
         if (!a.lut_prepacked)
             return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: h = A x in the kernel needs the prepacked layout");
         if (!xvec || (reinterpret_cast<uintptr_t>(a.loraA) & 15) != 0)

@@ -37,9 +37,26 @@ int fold_slots(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, 
     }
 }
 
+// 17..32 tokens: rank <= 16 only
+template <typename T>
+int fold32(const GemvParams& p, bool xsmem, int ctas, int cs, cudaStream_t stream, int* fit) {
+    switch (codebook_slots(p.G)) {
+        case 0:
+            return xsmem ? launch_variant<T, 4, 0, true, true, true, 1>(p, ctas, cs, stream, fit)
+                         : launch_variant<T, 4, 0, true, true, false, 1>(p, ctas, cs, stream, fit);
+        case 2:
+            return xsmem ? launch_variant<T, 4, 2, true, true, true, 1>(p, ctas, cs, stream, fit)
+                         : launch_variant<T, 4, 2, true, true, false, 1>(p, ctas, cs, stream, fit);
+        default:
+            return xsmem ? launch_variant<T, 4, 4, true, true, true, 1>(p, ctas, cs, stream, fit)
+                         : launch_variant<T, 4, 4, true, true, false, 1>(p, ctas, cs, stream, fit);
+    }
+}
+
 template <typename T>
 int fold_tokens(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int cs, cudaStream_t stream,
                 int* fit) {
+    if (p.M > 16) return fold32<T>(p, xsmem, ctas, cs, stream, fit);
     return p.M <= 8 ? fold_slots<T, 1>(p, rt, xsmem, false, ctas, cs, stream, fit)
                     : fold_slots<T, 2>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
 }

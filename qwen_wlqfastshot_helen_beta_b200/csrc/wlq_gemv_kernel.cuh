@@ -12,6 +12,7 @@ constexpr int kWarps = 4;
 constexpr int kRowsPerTile = 16;
 constexpr int kChunk = 128;  // k columns per warp iteration
 constexpr int kMaxTp = 8;    // ranks of a fused all-reduce
+constexpr int kMaxGemvM = 32;  // token rows of one launch: 1, 2 or 4 eight-token MMA tiles
 
 struct GemvParams {
     const uint32_t* q;

@@ -48,17 +48,18 @@ struct LinearArgs {
 struct TpLayout {
     size_t err, counters, flags, data, total;
 };
-inline TpLayout tp_layout(int world, int max_N) {
-    auto up = [](size_t v, size_t a) { return (v + a - 1) / a * a; };
+constexpr size_t tp_round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+constexpr TpLayout tp_layout(int world, int max_N) {
     const size_t tiles = (size_t)(max_N + 15) / 16;
-    TpLayout l;
+    TpLayout l{};
     l.err = 0;
     l.counters = 128;
-    l.flags = up(l.counters + 4 * tiles, 128);
-    l.data = up(l.flags + 4 * tiles * (size_t)world, 256);
-    l.total = up(l.data + 2ull * world * 16 * (size_t)max_N * 4, 256);
+    l.flags = tp_round_up(l.counters + 4 * tiles, 128);
+    l.data = tp_round_up(l.flags + 4 * tiles * (size_t)world, 256);
+    l.total = tp_round_up(l.data + 2ull * world * 16 * (size_t)max_N * 4, 256);
     return l;
 }
+
 
 int launch_gemv(const LinearArgs& a, cudaStream_t stream);
 int launch_gemm(const LinearArgs& a, cudaStream_t stream);
@@ -76,5 +77,10 @@ int read_device_error(int device, unsigned int* flags, int clear);
 
 // Multiprocessor count of the current device (cached per device).
 int device_sm_count();
+
+// Whether M tokens of an [N, K] layer run on the GEMV-class kernel (M <= 16;
+// 17..32 when the prepacked layout and 16-byte rows allow it and the
+// tensor-core GEMM would not fill the device) rather than the GEMM.
+bool gemv_preferred(int M, int N, int K, bool prepacked, const void* x);
 
 }  // namespace wlq

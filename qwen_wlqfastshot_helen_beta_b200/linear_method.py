@@ -482,8 +482,7 @@ class WLQLinearMethod(LinearMethodBase):
             A = self._lora_A(layer, x2.dtype)
             # decode: the GEMV computes h = A x itself (one launch instead of
             # F.linear + .float() + GEMV) when its layout allows
-            if M <= 16 and fmt == 1 and 0 < lora_B.shape[1] <= 32 and layer.K % 8 == 0 and \
-                    x2.data_ptr() % 16 == 0 and A.data_ptr() % 16 == 0:
+            if A.data_ptr() % 16 == 0 and _C.folds_h(M, layer.N, layer.K, int(lora_B.shape[1]), fmt, x2):
                 lora_A = A
             else:
                 lora_h = F.linear(x2, A).float()

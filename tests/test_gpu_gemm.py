@@ -44,18 +44,18 @@ def test_gemm_matches_oracle(case, dtype):
     rng = np.random.default_rng(7 * N + K + G)
     L = make_np_layer(rng, N, K, G, goff, density=0.02, outliers=outl, dora=dora)
     T = dev_layer(L)
-    for M in (17, 128, 200, 300):
+    for M in (17, 24, 32, 128, 200, 300):
         x, h = inputs(rng, L, M, dtype)
         ref = reference_output(L, x.float().cpu().numpy(), None if h is None else h.cpu().numpy())
         ys = []
-        for fmt in (0, 1):
+        for fmt in (0, 1):  # up to 32 tokens the prepacked layout runs on the GEMV-class kernel
             y = run_ours(L, T, x, h, fmt=fmt)
             assert torch.isfinite(y).all(), (M, fmt)
             e = rel_err(y.float().cpu().numpy(), ref)
             assert e <= TOL[dtype], (M, fmt, e)
             ys.append(y.float())
-        # the two layouts patch the same outlier values into the tile
-        assert rel_err(ys[1].cpu().numpy(), ys[0].cpu().numpy()) <= 1e-3, M
+        if M > 32:  # the two layouts patch the same outlier values into the tile
+            assert rel_err(ys[1].cpu().numpy(), ys[0].cpu().numpy()) <= 1e-3, M
 
 
 def test_gemm_outlier_edges():
@@ -113,6 +113,28 @@ def test_gemm_full_size_shapes(name, M):
     ref = (x.float() @ W.float().t() + L.lora_scale * (h @ L.lora_B.float().t())) * L.dora_gamma.float()
     e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
     assert e <= 2e-2, (name, M, e)
+
+
+@pytest.mark.parametrize("name,M", [("qkv", 24), ("o", 32), ("down", 32), ("gate_up", 32)])
+def test_decode_batch_17_to_32(name, M):
+    """Decode batches of 17..32 tokens at BASELINE shapes through wlq_gemm:
+    the GEMV-class kernel (four 8-token MMA tiles) where the tensor-core
+    GEMM would not fill the device (qkv, o, down), the GEMM otherwise
+    (gate_up); against the dequantised weights in fp32."""
+    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+    K, N = S.QWEN25_7B[name]
+    L = S.make_layer(N, K, group_size=128, density=0.005, r=16, seed=21).prepack(torch.bfloat16)
+    W = torch.empty((N, K), dtype=torch.float16, device="cuda")
+    C().dequant_w0(L.q_packed, L.lut_c, W, N, K, 4, L.words_per_row, L.chunk_offsets, L.chunk_cols, L.chunk_vals,
+                   128, 0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(6)
+    x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+    h = S.lora_h(L, x)
+    ref = (x.float() @ W.float().t() + L.lora_scale * (h @ L.lora_B.float().t())) * L.dora_gamma.float()
+    for y in (S.forward(L, x, h=h), S.forward_fold(L, x)):
+        e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
+        assert e <= 2e-2, (name, M, e)
 
 
 @pytest.mark.parametrize("N,K,M", [(9472, 1024, 512), (4608, 3584, 2048), (3584, 1024, 512)])

@@ -117,7 +117,7 @@ def test_gemv_lora_a_matches_oracle(case, dtype):
     cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], L.N, L.K, 4, dtype, L.G,
                                       L.goff)
     A = T["A"].to(dtype).contiguous()
-    for M in (1, 2, 5, 8, 9, 16):
+    for M in (1, 2, 5, 8, 9, 16) + ((17, 32) if r <= 16 else ()):
         x, h = inputs(rng, L, M, dtype)
         ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
         y = torch.full((M, N), float("nan"), dtype=dtype, device="cuda")
@@ -127,8 +127,9 @@ def test_gemv_lora_a_matches_oracle(case, dtype):
         assert torch.isfinite(y).all(), M
         e = rel_err(y.float().cpu().numpy(), ref)
         assert e <= TOL[dtype], (M, e)
-        y_h = run_ours(L, T, x, h, gemv=(M == 1), fmt=1)
-        assert rel_err(y.float().cpu().numpy(), y_h.float().cpu().numpy()) <= 1e-2, M
+        if M <= 16:
+            y_h = run_ours(L, T, x, h, gemv=(M == 1), fmt=1)
+            assert rel_err(y.float().cpu().numpy(), y_h.float().cpu().numpy()) <= 1e-2, M
 
 
 def test_gemv_lora_a_rejects():
@@ -268,7 +269,7 @@ def test_full_size_shapes(name):
         assert e <= 2e-2, (name, M, e)
     # the GEMV computing h = A x itself (the decode path apply() takes), every token count
     L.prepack(torch.bfloat16)
-    for M in range(1, 17):
+    for M in range(1, 33):
         x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
         h = S.lora_h(L, x)
         y = S.forward_fold(L, x)
