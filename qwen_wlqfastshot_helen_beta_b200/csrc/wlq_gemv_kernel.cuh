@@ -210,45 +210,68 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
     // codebook group of a column (clamped: columns past K meet zero activations)
     auto group_at = [&](int col) { return min((col + p.goff) >> p.log2G, p.ngroups - 1); };
 
+    // The lane's part of every ring copy is fixed for the whole K range: the
+    // 16-byte piece q4 = lane % 4 of index rows lane / 4 and lane / 4 + 8, its
+    // codebook slot and half, and (computing h) its rows of A.  Their element
+    // offsets from the tensors' starts are computed once, so a chunk only adds
+    // its stride.
+    const int q4 = lane & 3;
+    const int ir = lane >> 2;
+    const bool iok0 = tile_row0 + ir < p.N, iok1 = tile_row0 + ir + 8 < p.N;
+    const uint32_t ioff0 = iok0 ? (uint32_t)(tile_row0 + ir) * (uint32_t)p.wpr + 4u * q4 : 0u;
+    const uint32_t ioff1 = iok1 ? (uint32_t)(tile_row0 + ir + 8) * (uint32_t)p.wpr + 4u * q4 : 0u;
+    const uint32_t idst = (uint32_t)(ir * 64 + q4 * 16);
+    constexpr int kSlots = GROUPED ? NSLOT : 1;
+    const int ls = (lane >> 1) % kSlots, lhalf = lane & 1;  // codebook slot and half of this lane
+    bool lok[kSlots];
+    uint32_t loff[kSlots], ldst[kSlots];
+#pragma unroll
+    for (int i = 0; i < kSlots; ++i) {
+        const int r = (lane + 32 * i) / (2 * kSlots);
+        lok[i] = tile_row0 + r < p.N;
+        loff[i] = lok[i] ? ((uint32_t)(tile_row0 + r) * (uint32_t)p.ngroups + ls) * 16u + 8u * lhalf : 0u;
+        ldst[i] = (uint32_t)(R::kIdxBytes + (r * kSlots + ls) * 32 + lhalf * 16);
+    }
+    constexpr int kAPieces = RT > 0 ? 2 * RT : 1;
+    uint32_t aoff[kAPieces];
+    bool aok[kAPieces];
+#pragma unroll
+    for (int i = 0; i < kAPieces; ++i) {
+        const int ar = ir + 8 * i;
+        aok[i] = RT > 0 && ar < p.r;
+        aoff[i] = aok[i] ? (uint32_t)ar * (uint32_t)p.K + 32u * warp + 8u * q4 : 0u;
+    }
+
     // chunk c into ring stage st; one commit group per lane per chunk, empty
     // past the rank's range
     auto issue = [&](int c, int st) {
         if (c < c_end) {
             const uint32_t base = ring + (uint32_t)(st * R::kStageBytes);
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int pc = lane + 32 * i;
-                const int r = pc >> 2, q4 = pc & 3;
-                const int row = tile_row0 + r;
-                const int wi = c * (kChunk / 8) + 4 * q4;
-                const bool ok = row < p.N && wi < p.wpr;
-                cp_async16(base + r * 64 + q4 * 16, p.q + (ok ? (int64_t)row * p.wpr + wi : 0), ok);
-            }
+            const uint32_t wi = (uint32_t)c * (kChunk / 8);  // first index word of the chunk
+            const bool wok = (int)(wi + 4u * q4) < p.wpr;
+            const bool ok0 = iok0 && wok, ok1 = iok1 && wok;
+            cp_async16(base + idst, p.q + (ok0 ? ioff0 + wi : 0u), ok0);
+            cp_async16(base + idst + 8 * 64, p.q + (ok1 ? ioff1 + wi : 0u), ok1);
             if constexpr (GROUPED) {
                 const int g0 = group_at(c * kChunk);
                 const int used = group_at(c * kChunk + kChunk - 1) - g0 + 1;
+                const bool sok = ls < used;
 #pragma unroll
                 for (int i = 0; i < NSLOT; ++i) {
-                    const int pc = lane + 32 * i;
-                    const int r = pc / (2 * NSLOT), s = (pc >> 1) % NSLOT, half = pc & 1;
-                    const int row = tile_row0 + r;
-                    const bool ok = row < p.N && s < used;
-                    cp_async16(base + R::kIdxBytes + (r * NSLOT + s) * 32 + half * 16,
-                               p.lut + (ok ? ((int64_t)row * p.ngroups + g0 + s) * 16 + 8 * half : 0), ok);
+                    const bool ok = lok[i] && sok;
+                    cp_async16(base + ldst[i], p.lut + (ok ? loff[i] + (uint32_t)g0 * 16u : 0u), ok);
                 }
             }
             if constexpr (RT > 0) {
                 // rows [0, 16 RT) of A, columns [128c + 32w, +32); rows past r
                 // and columns past K (K % 8 == 0) read as zero
-                const int col0 = c * kChunk + 32 * warp;
+                const uint32_t ca = (uint32_t)c * kChunk;
+                const bool cok = (int)(ca + 32u * warp + 8u * q4) < p.K;
 #pragma unroll
                 for (int i = 0; i < 2 * RT; ++i) {
-                    const int pc = lane + 32 * i;
-                    const int ar = pc >> 2, q4 = pc & 3;
-                    const int col = col0 + 8 * q4;
-                    const bool ok = ar < p.r && col < p.K;
-                    cp_async16(base + R::kIdxBytes + R::kPlaneBytes + ar * 64 + q4 * 16,
-                               p.loraA + (ok ? (int64_t)ar * p.K + col : 0), ok);
+                    const bool ok = aok[i] && cok;
+                    cp_async16(base + R::kIdxBytes + R::kPlaneBytes + (ir + 8 * i) * 64 + q4 * 16,
+                               p.loraA + (ok ? aoff[i] + ca : 0u), ok);
                 }
             }
         }
