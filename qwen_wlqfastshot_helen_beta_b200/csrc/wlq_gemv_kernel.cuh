@@ -209,6 +209,11 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 
     // codebook group of a column (clamped: columns past K meet zero activations)
     auto group_at = [&](int col) { return min((col + p.goff) >> p.log2G, p.ngroups - 1); };
+    // codebook slot of this lane's 32 columns within a chunk: the same for
+    // every chunk when groups are at most a chunk wide (a chunk then starts on
+    // a group boundary plus goff % G).  Columns past K may land on a slot the
+    // chunk did not load; it was zero-filled and their activations are zero.
+    const int lane_slot = p.G <= kChunk ? ((p.goff & (p.G - 1)) + 32 * t) >> p.log2G : 0;
 
     // The lane's part of every ring copy is fixed for the whole K range: the
     // 16-byte piece q4 = lane % 4 of index rows lane / 4 and lane / 4 + 8, its
@@ -490,7 +495,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
         const uint4 w1 = lds128(base + (g + 8) * 64 + 16 * t);
         LutPlanes P0, P1;
         if (GROUPED) {
-            const int s = group_at(c * kChunk + 32 * t) - group_at(c * kChunk);
+            const int s = p.G <= kChunk ? lane_slot : group_at(c * kChunk + 32 * t) - group_at(c * kChunk);
             const uint32_t pb = base + R::kIdxBytes + s * 32;
             planes_from_smem<T, PREPACKED>(pb + g * (NSLOT * 32), P0);
             planes_from_smem<T, PREPACKED>(pb + (g + 8) * (NSLOT * 32), P1);
