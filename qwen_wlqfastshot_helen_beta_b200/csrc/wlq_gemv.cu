@@ -168,8 +168,7 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
         const TpLayout l = tp_layout(a.tp_world, a.tp_nmax);
         for (int q = 0; q < a.tp_world; ++q) {
             char* b = static_cast<char*>(a.tp_bufs[q]);
-            p.tp_data[q] = reinterpret_cast<float*>(b + l.data);
-            p.tp_flags[q] = reinterpret_cast<uint32_t*>(b + l.flags);
+            p.tp_data[q] = reinterpret_cast<unsigned long long*>(b + l.data);
         }
         char* mine = static_cast<char*>(a.tp_bufs[a.tp_rank]);
         p.tp_counters = reinterpret_cast<uint32_t*>(mine + l.counters);

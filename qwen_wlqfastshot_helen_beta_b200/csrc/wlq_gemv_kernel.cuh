@@ -36,8 +36,8 @@ struct GemvParams {
     uint32_t mul16, mul31; // 1<<16 and 1<<31, runtime values so mul.hi stays a multiply
     // fused tensor-parallel all-reduce (row-parallel layers), tp_world > 1
     int tp_world, tp_rank, tp_nmax;
-    float* tp_data[kMaxTp];      // each rank's slots [2 parities][world][16 tokens][tp_nmax] fp32
-    uint32_t* tp_flags[kMaxTp];  // each rank's per-tile epochs [tiles][world]
+    unsigned long long* tp_data[kMaxTp];  // each rank's slots [2 parities][world][16 tokens][tp_nmax]:
+                                          // fp32 value bits | epoch << 32
     uint32_t* tp_counters;       // this rank's per-tile call counters [tiles]
     uint32_t* tp_err;            // this rank's error word
 };
@@ -105,72 +105,80 @@ struct Ring {
     static constexpr int kStageBytes = kIdxBytes + kPlaneBytes + kABytes;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+// 8-byte slot accesses that reach the other GPUs' memory and are never
+// cached or merged: one store carries a value and its epoch together.
+__device__ __forceinline__ void st_slot(unsigned long long* a, unsigned long long v) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+__device__ __forceinline__ unsigned long long ld_slot(const unsigned long long* a) {
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
     return v;
 }
 
 // Row-parallel epilogue with the all-reduce fused, for one warp's 16-row
-// tile (cluster rank 0): the tile's gamma-scaled partial results are pushed
-// into slot [parity][this rank] of every rank's buffer over NVLink peer
-// stores, the tile's epoch is published to every rank with a system-scope
-// release store, and once every rank's epoch for the tile has arrived
-// (bounded wait) the local slots are summed into out.  Epochs come from a
-// per-tile call counter that advances identically on every rank, so CUDA
-// graph replays need no host input; slots alternate by epoch parity, and a
-// rank cannot run two calls ahead on a tile because each call waits for all
-// ranks' data of the previous one.
+// tile (cluster rank 0).  Each of the tile's gamma-scaled partial values goes
+// to every other rank as ONE 8-byte store holding the value and the call's
+// epoch, so a reader knows a slot is complete once its epoch matches: no
+// fences and no separate flags on the way (a system-scope fence per tile cost
+// ~25 us per call over NVLink).  Epochs come from a per-tile call counter that
+// advances identically on every rank, so CUDA graph replays need no host
+// input; slots alternate by epoch parity, and a rank cannot run two calls
+// ahead on a tile because each call waits for all ranks' values of the
+// previous one.  Every rank adds the ranks' values in rank order, so all ranks
+// hold the same result bit for bit.  The waits share one 2 s deadline; when
+// it passes the error word is set and the output is undefined.
 template <typename T, int MT>
 __device__ void tp_allreduce_tile(const GemvParams& p, float (*part)[MT], uint32_t nranks, int tile_row0, int lane,
                                   float gam) {
+    constexpr int kPer = (kRowsPerTile * MT + 31) / 32;  // tile elements per lane
     const int tile = tile_row0 / kRowsPerTile;
     const int world = p.tp_world, me = p.tp_rank;
-    const bool clustered = nranks > 1;
     uint32_t cnt = lane == 0 ? p.tp_counters[tile] + 1u : 0u;
     cnt = __shfl_sync(0xFFFFFFFFu, cnt, 0);
     const int par = (int)(cnt & 1u);
-    for (int e = lane; e < kRowsPerTile * MT; e += 32) {
+    const unsigned long long tag = (unsigned long long)cnt << 32;
+    float own[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int e = lane + 32 * i;
         const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
         const int n = tile_row0 + rl;
-        if (n >= p.N || tk >= p.M) continue;
-        const float s = cluster_sum(&part[rl][tk], clustered ? nranks : 1u) * gam;
+        own[i] = 0.f;
+        if (e >= kRowsPerTile * MT || n >= p.N || tk >= p.M) continue;
+        own[i] = cluster_sum(&part[rl][tk], nranks) * gam;
         const int64_t slot = ((int64_t)(par * world + me) * kRowsPerTile + tk) * p.tp_nmax + n;
-        for (int q = 0; q < world; ++q) p.tp_data[q][slot] = s;
+        for (int q = 0; q < world; ++q)
+            if (q != me) st_slot(p.tp_data[q] + slot, tag | __float_as_uint(own[i]));
     }
-    __threadfence_system();  // this lane's peer stores before the epoch
-    __syncwarp();
-    int ok = 1;
-    if (lane == 0) {
-        for (int q = 0; q < world; ++q) st_release_sys(p.tp_flags[q] + tile * world + me, cnt);
-        const uint32_t* mine = p.tp_flags[me] + tile * world;
-        const uint64_t t0 = globaltimer_ns();
-        for (int q = 0; q < world && ok; ++q) {
-            while (ld_acquire_sys(mine + q) < cnt) {
-                if (globaltimer_ns() - t0 > 2000000000ull) {  // a rank never arrived: give up
-                    atomicOr(p.tp_err, 1u);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        p.tp_counters[tile] = cnt;
-    }
-    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-    __threadfence();
-    if (!ok) return;
-    for (int e = lane; e < kRowsPerTile * MT; e += 32) {
+    const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int e = lane + 32 * i;
         const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
         const int n = tile_row0 + rl;
-        if (n >= p.N || tk >= p.M) continue;
+        if (e >= kRowsPerTile * MT || n >= p.N || tk >= p.M) continue;
         float s = 0.f;
-        for (int q = 0; q < world; ++q)
-            s += __ldcg(p.tp_data[me] + ((int64_t)(par * world + q) * kRowsPerTile + tk) * p.tp_nmax + n);
+        for (int q = 0; q < world; ++q) {
+            if (q == me) {
+                s += own[i];
+                continue;
+            }
+            const unsigned long long* a =
+                p.tp_data[me] + ((int64_t)(par * world + q) * kRowsPerTile + tk) * p.tp_nmax + n;
+            unsigned long long w = ld_slot(a);
+            while ((uint32_t)(w >> 32) != cnt && ok) {
+                if (globaltimer_ns() > deadline) ok = false;  // a rank never arrived: give up
+                else w = ld_slot(a);
+            }
+            s += __uint_as_float((uint32_t)w);
+        }
         reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s);
     }
+    if (!ok) atomicOr(p.tp_err, 1u);
+    __syncwarp();
+    if (lane == 0) p.tp_counters[tile] = cnt;
 }
 
 // RT > 0: the low-rank input h = A x (r <= 16 RT) is computed here.  In

@@ -43,10 +43,11 @@ struct LinearArgs {
 };
 
 // Layout of a tensor-parallel communication buffer (one per rank, shared
-// through CUDA IPC): error word, per-tile call counters (local use), per-tile
-// epochs written by every rank, then [2][world][16][max_N] fp32 slots.
+// through CUDA IPC): error word, per-tile call counters (local use), then
+// [2][world][16][max_N] 8-byte slots, each an fp32 value and the epoch of the
+// call that wrote it.
 struct TpLayout {
-    size_t err, counters, flags, data, total;
+    size_t err, counters, data, total;
 };
 constexpr size_t tp_round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 constexpr TpLayout tp_layout(int world, int max_N) {
@@ -54,9 +55,8 @@ constexpr TpLayout tp_layout(int world, int max_N) {
     TpLayout l{};
     l.err = 0;
     l.counters = 128;
-    l.flags = tp_round_up(l.counters + 4 * tiles, 128);
-    l.data = tp_round_up(l.flags + 4 * tiles * (size_t)world, 256);
-    l.total = tp_round_up(l.data + 2ull * world * 16 * (size_t)max_N * 4, 256);
+    l.data = tp_round_up(l.counters + 4 * tiles, 256);
+    l.total = tp_round_up(l.data + 2ull * world * 16 * (size_t)max_N * 8, 256);
     return l;
 }
 
