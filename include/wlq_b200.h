@@ -152,9 +152,11 @@ WLQ_API int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device);
 /* ------------------------------------------------ tensor parallelism --- */
 /* Row-parallel layers (o, down) need the sum of every rank's partial output.
  * wlq_gemv_allreduce fuses that all-reduce into the GEMV epilogue over NVLink
- * peer memory: each rank pushes its gamma-scaled tile into every rank's
- * communication buffer, publishes a per-tile epoch, waits (bounded, 2 s) for
- * all ranks' epochs and sums.  Each rank allocates one buffer of
+ * peer memory: each rank stores its gamma-scaled tile into every other rank's
+ * communication buffer, every value tagged with the call's epoch in the same
+ * 8-byte store, then waits (bounded, 2 s) until its own slots hold every
+ * rank's values of this epoch and sums them in rank order.  Each rank
+ * allocates one buffer of
  * wlq_tp_buffer_bytes(world, max_N) with wlq_tp_buffer_alloc, exchanges the
  * 64-byte IPC handles with the other ranks (any host channel) and maps theirs
  * with wlq_tp_buffer_open.  All ranks must issue the same sequence of calls.
