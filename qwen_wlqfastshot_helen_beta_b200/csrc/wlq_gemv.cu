@@ -215,17 +215,24 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
                     : dispatch<__half>(p, a.lut_prepacked, xvec, pl.xsmem, ctas, pl.cs, stream, fit);
     };
 
-    // Split K over a cluster until about 4 CTAs (16 warps) per SM are in
-    // flight, keeping at least 2 chunks per rank; then take the largest split
+    // Split K over a cluster (up to 16 CTAs) until about 4 CTAs (16 warps)
+    // per SM are in flight, keeping at least 2 chunks per rank, and at least 4
+    // above 8 ranks (measured: a 14-way split of 28 chunks lost to the wider
+    // reduction, a 16-way split of 148 won 15 %); then take the largest split
     // (down to none) whose clusters the device holds in one wave.
     const int sms = device_sm_count();
+    auto chunks_ok = [&](int cs) { return p.kchunks >= (cs > 8 ? 4 : 2) * cs; };
     int cs_max = 1;
-    while (cs_max < 8 && (int64_t)ctas * cs_max < 4LL * sms && p.kchunks >= 2 * (cs_max + 1)) ++cs_max;
+    while (cs_max < kMaxSplit && (int64_t)ctas * cs_max < 4LL * sms && chunks_ok(cs_max + 1)) ++cs_max;
     Plan pl = configure(1);
     for (int cs = cs_max; cs > 1; --cs) {
         const Plan c = configure(cs);
         int fit = 0;
         const int rc = run(c, &fit);
+        if (rc && cs > 8) {  // a non-portable cluster size the device or driver refused: try smaller
+            cudaGetLastError();
+            continue;
+        }
         if (rc) return rc;
         if (ctas <= fit) {
             pl = c;

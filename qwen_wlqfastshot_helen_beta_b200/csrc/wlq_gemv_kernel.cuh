@@ -13,6 +13,7 @@ constexpr int kRowsPerTile = 16;
 constexpr int kChunk = 128;  // k columns per warp iteration
 constexpr int kMaxTp = 8;    // ranks of a fused all-reduce
 constexpr int kMaxGemvM = 32;  // token rows of one launch: 1, 2 or 4 eight-token MMA tiles
+constexpr int kMaxSplit = 16;  // CTAs of a K-split cluster (above 8: a non-portable cluster size)
 
 struct GemvParams {
     const uint32_t* q;
@@ -82,12 +83,13 @@ __device__ __forceinline__ void stage_x_issue(uint16_t* xs, const T* __restrict_
 __device__ __forceinline__ float cluster_sum(const float* own, uint32_t nranks) {
     if (nranks == 1) return *own;
     const uint32_t a = smem_u32(own);
-    float v[8];
+    float v[kMaxSplit];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) v[q] = (uint32_t)q < nranks ? ld_shared_cluster_f32(mapa_shared(a, (uint32_t)q)) : 0.f;
+    for (int q = 0; q < kMaxSplit; ++q)
+        v[q] = (uint32_t)q < nranks ? ld_shared_cluster_f32(mapa_shared(a, (uint32_t)q)) : 0.f;
     float s = v[0];
 #pragma unroll
-    for (int q = 1; q < 8; ++q) s += v[q];
+    for (int q = 1; q < kMaxSplit; ++q) s += v[q];
     return s;
 }
 
@@ -676,6 +678,10 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, i
     if (smem + kStatic > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return check_cuda(e, "gemv_kernel smem attribute");
+    }
+    if (cs > 8) {  // clusters above the portable size of 8
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return check_cuda(e, "gemv_kernel cluster size attribute");
     }
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
