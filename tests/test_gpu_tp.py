@@ -68,6 +68,24 @@ def _rank_main(rank, port, results):
                 y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
                 fused(x, h, y, in_kernel_h=i % 2 == 1)
                 check(x, h, y)
+        # a down-proj shard (K = 9472 per rank): the K split takes a cluster of
+        # more than 8 CTAs, whose reduction feeds the exchange
+        Kd = 9472
+        Ld = S.make_layer(N, Kd, group_size=128, density=0.005, r=16, seed=60 + rank, device=dev)
+        Ld.prepack(torch.bfloat16)
+        lutd, colsd, valsd, fmtd = Ld.operands_for(torch.bfloat16)
+        for M in (1, 16):
+            x = torch.randn((M, Kd), generator=gen, device=dev).to(torch.bfloat16)
+            h = S.lora_h(Ld, x)
+            y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            _C.gemv_allreduce(comm, x, Ld.q_packed, lutd, y, N, Kd, 4, Ld.words_per_row, Ld.chunk_offsets, colsd,
+                              valsd, None, Ld.lora_B, Ld.dora_gamma, Ld.lora_scale, Ld.group_size, Ld.group_offset,
+                              fmtd, lora_A=Ld.lora_A_act)
+            own = S.forward(Ld, x, h=h).float()
+            parts = [torch.empty_like(own) for _ in range(2)]
+            dist.all_gather(parts, own)
+            ref = parts[0] + parts[1]
+            errs.append(float((y.float() - ref).abs().max() / ref.abs().max()))
         # the same inside a CUDA graph, replayed with new inputs
         M = 8
         x = torch.randn((M, Kp), generator=gen, device=dev).to(torch.bfloat16)
