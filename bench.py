@@ -255,16 +255,16 @@ def run_ours(args):
                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         _lib.check(rc, "wlq_gemv_lora_a")
 
-    def launch_gemm(L, x, h, out):
-        """One prefill call (M > 16) given h = A x."""
-        rc = lib.wlq_gemm(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(L.q_packed.data_ptr()),
-                          ctypes.c_void_p(L.lut_packed.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-                          ctypes.c_void_p(L.chunk_offsets.data_ptr()), ctypes.c_void_p(L.cols_packed.data_ptr()),
-                          ctypes.c_void_p(L.delta_packed.data_ptr()), ctypes.c_void_p(h.data_ptr()),
-                          ctypes.c_void_p(L.lora_B.data_ptr()), ctypes.c_void_p(L.dora_gamma.data_ptr()),
-                          L.lora_scale, L.r, x.shape[0], L.N, L.K, 4, L.words_per_row, L.group_size,
-                          L.group_offset, _lib.WLQ_LUT_PREPACKED, _lib.WLQ_DTYPE_BF16,
-                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    def launch_gemm(L, x, H, out):
+        """One prefill call (M > 16) as the op runs it: H = X A^T on this
+        package's kernel (wlq_lora_h), then the tensor-core GEMM."""
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rc = lib.wlq_lora_h(vp(x), vp(L.lora_A_act), vp(H), x.shape[0], L.K, L.r, _lib.WLQ_DTYPE_BF16, st)
+        _lib.check(rc, "wlq_lora_h")
+        rc = lib.wlq_gemm(vp(x), vp(L.q_packed), vp(L.lut_packed), vp(out), vp(L.chunk_offsets), vp(L.cols_packed),
+                          vp(L.delta_packed), vp(H), vp(L.lora_B), vp(L.dora_gamma), L.lora_scale, L.r, x.shape[0],
+                          L.N, L.K, 4, L.words_per_row, L.group_size, L.group_offset, _lib.WLQ_LUT_PREPACKED,
+                          _lib.WLQ_DTYPE_BF16, st)
         _lib.check(rc, "wlq_gemm")
 
     def reduce_if_rowpar(name, out):  # NCCL only without the fused path
@@ -318,7 +318,14 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    align = torch.zeros(1, device=dev)
     with ClockSampler(local) as clk:
+        if world > 1:
+            # start every rank's timed region together: a spin kernel keeps the
+            # stream busy while the host enqueues, then a one-element all-reduce
+            # completes at nearly the same moment on every rank, before t0
+            torch.cuda._sleep(4_000_000)
+            dist.all_reduce(align)
         t0.record()
         g_time.replay()
         t1.record()
@@ -439,11 +446,18 @@ def run_ours(args):
     e2e_value = step_bytes_job * args.steps / (e2e_ms * 1e-3) / 1e9
     eager_value = step_bytes_job * args.steps / (eager_ms * 1e-3) / 1e9
 
-    gemm = gemm_leg(layers, dev, launch_gemm, peaks, peaks_kind, local) if world == 1 else None
+    gemm = gemm_leg(layers, dev, launch_gemm, peaks, peaks_kind, local, world, rank)
+    config0 = ref_gpu = None
+    if world == 1 and not args.no_baselines:
+        config0 = cpu_baseline_config0(dev, args.cpu_budget)
+        ref_gpu = reference_gpu_baseline(dev, peaks)
 
     result = None
     if rank == 0:
-        achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
+        # the dominant kernel's achieved bandwidth, from the headline graph
+        # (its launches back to back, no event nodes): algorithmic bytes of
+        # this rank's launches / this rank's share of the timed region
+        achieved = step_bytes_rank * args.steps / (elapsed_ms * 1e-3) / 1e9
         peak = float(peaks["hbm_gbs"])
         traffic = None
         tp = os.path.join(ROOT, "profiles", "gemv_traffic.json")
@@ -471,7 +485,12 @@ def run_ours(args):
                 else "fallback 6650 GB/s",
                 "kernel": "gemv_kernel with h = A x in the kernel (wlq_gemv_kernel.cuh), all 16 (linear, M) "
                           "launches of a step",
+                "timing": "headline graph (the step's launches back to back); achieved = this GPU's algorithmic "
+                          "bytes per step / ms_per_step, so kernel time per step <= ms_per_step",
                 "per_config_gbs": {k: round(v[1] / (v[0] * 1e-3) / 1e9, 1) for k, v in per_cfg.items()},
+                "per_config_timing": "a second graph of the same steps with an event pair around every launch "
+                                     "(event nodes serialise and add time: a lower bound per launch)",
+                "event_graph_gbs": round(kern_bytes / (kern_ms * 1e-3) / 1e9, 1),
             },
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
@@ -485,6 +504,10 @@ def run_ours(args):
         }
         if gemm is not None:
             result["gemm"] = gemm
+        if config0 is not None:
+            result["cpu_baseline_config0"] = config0
+        if ref_gpu is not None:
+            result["reference_gpu_baseline"] = ref_gpu
     if world > 1:
         del g_warm, g_time, g_kern, g_e2e
         torch.cuda.synchronize()
@@ -498,12 +521,16 @@ def run_ours(args):
     return result, layers if rank == 0 else None
 
 
-def gemm_leg(layers, dev, launch, peaks, peaks_kind, local, reps=10, warmup=3):
-    """the prefill GEMM (tcgen05 kernel, wlq_gemm.cu) on the
-    four linears at M in GEMM_MS, each (linear, M) a CUDA graph of `reps`
-    launches timed with events; TFLOPS = 2 M N K / time."""
+def gemm_leg(layers, dev, launch, peaks, peaks_kind, local, world=1, rank=0, reps=10, warmup=3):
+    """the prefill op (H = X A^T on wlq_lora_h, then the
+    tcgen05 GEMM of wlq_gemm.cu) on the four linears at M in GEMM_MS, each
+    (linear, M) a CUDA graph of `reps` calls timed with events; TFLOPS =
+    2 M N K / time.  With world > 1 each rank runs its tensor-parallel shard
+    (qkv / gate_up by rows, o / down by K) and the row-parallel layers end
+    with an NCCL all-reduce of [M, N] inside the graph, as vLLM runs them;
+    times are the max over ranks, TFLOPS count the unsharded layer."""
     import torch
-    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+    import torch.distributed as dist
     gen = torch.Generator(device=dev)
     gen.manual_seed(77)
     cfgs = []
@@ -511,80 +538,364 @@ def gemm_leg(layers, dev, launch, peaks, peaks_kind, local, reps=10, warmup=3):
         L = layers[0][name]
         for M in GEMM_MS:
             x = torch.randn((M, L.K), generator=gen, device=dev).to(torch.bfloat16)
-            cfgs.append((name, M, L, x, S.lora_h(L, x), torch.empty((M, L.N), dtype=torch.bfloat16, device=dev)))
+            H = torch.empty((M, L.r), dtype=torch.float32, device=dev)
+            cfgs.append((name, M, K, N, L, x, H, torch.empty((M, L.N), dtype=torch.bfloat16, device=dev)))
+    rowpar = lambda name: world > 1 and name in ("o", "down")  # noqa: E731
     for _ in range(warmup):
-        for (_, _, L, x, h, out) in cfgs:
-            launch(L, x, h, out)
+        for (name, M, K, N, L, x, H, out) in cfgs:
+            launch(L, x, H, out)
+            if rowpar(name):
+                dist.all_reduce(out)
     torch.cuda.synchronize()
-    graphs = []
-    for (name, M, L, x, h, out) in cfgs:
+
+    def graph_of(L, x, H, out, with_ar):
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
                 for _ in range(reps):
-                    launch(L, x, h, out)
+                    launch(L, x, H, out)
+                    if with_ar:
+                        dist.all_reduce(out)
         torch.cuda.current_stream().wait_stream(s)
-        graphs.append(g)
-    per, tot_ms, tot_flops = {}, 0.0, 0.0
+        return g
+
+    graphs = [graph_of(L, x, H, out, rowpar(name)) for (name, M, K, N, L, x, H, out) in cfgs]
+    kgraphs = [graph_of(L, x, H, out, False) if rowpar(name) else None for (name, M, K, N, L, x, H, out) in cfgs]
+
+    def timed(g):
+        g.replay()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    per, ar_share, tot_ms, tot_flops = {}, {}, 0.0, 0.0
     with ClockSampler(local) as clk:
-        for (name, M, L, x, h, out), g in zip(cfgs, graphs):
-            g.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            g.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / reps
-            fl = 2.0 * M * L.N * L.K
+        for cfg, g, kg in zip(cfgs, graphs, kgraphs):
+            name, M, K, N = cfg[:4]
+            ms = timed(g)
+            fl = 2.0 * M * N * K  # the unsharded layer
             per[f"{name}/M{M}"] = round(fl / (ms * 1e-3) / 1e12, 1)
+            if kg is not None:
+                ar_share[f"{name}/M{M}"] = round(max(0.0, 1.0 - timed(kg) / ms), 3)
             tot_ms += ms
             tot_flops += fl
     tflops = tot_flops / (tot_ms * 1e-3) / 1e12
     peak = float(peaks.get("bf16_tflops", 1590.0))
-    del graphs
-    return {
-        "metric": "GEMM TFLOPS (2*M*N*K / kernel time)",
+    del graphs, kgraphs
+    out = {
+        "metric": "GEMM TFLOPS (2*M*N*K / time of the prefill op: wlq_lora_h + wlq_gemm)",
         "value": round(tflops, 1), "unit": "TFLOP/s",
         "config": "BASELINE config 2: qkv/o/gate_up/down at M in {512, 2048, 8192}, bf16, group 128, "
                   "rank 16, 0.5% outliers; weights L2-resident across M tiles as in a real prefill",
         "ms_all_configs": round(tot_ms, 3),
         "per_config_tflops": per,
-        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(tflops / peak, 4),
+        "roofline": {"bound": "tensor", "achieved": round(tflops / world, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / world / peak, 4),
                      "peak_source": f"{peaks_kind} bf16_tflops (cuBLAS burst, MEASURED_PEAKS.json)"
                      if peaks_kind == "measured" else "fallback 1590 TFLOP/s",
-                     "kernel": "gemm_kernel (wlq_gemm.cu)"},
-        "gpu_launches": reps * len(cfgs),
+                     "kernel": "gemm_kernel (wlq_gemm.cu), with lora_h_kernel (wlq_lora_h.cu) in the timed op"},
+        "gpu_launches": 2 * reps * len(cfgs),
         "clocks": clk.summary(),
+    }
+    if world > 1:
+        out["parallelism"] = (f"tp{world}: qkv/gate_up split by output rows, o/down by K with an NCCL all-reduce "
+                              f"of [M, N] bf16 after the GEMM (in the timed graph); time = max over ranks")
+        out["tflops_per_gpu"] = round(tflops / world, 1)
+        out["allreduce_share"] = ar_share
+    return out
+
+
+def cpu_baseline_config0(dev, budget_s=15.0, reps=50):
+    """BASELINE config 0 (K=4864 -> N=896, M=8, fp32 activations, group-128
+    recipe): ms per call of this package's op the way WLQLinearMethod.apply
+    runs it (x cast to fp16, h = A x inside the GEMV, output cast back to
+    fp32), device-resident and end to end from pinned host memory, beside the
+    reference's CPU dequantize-then-matmul steps (oracle/cpu_baseline.py) on
+    the box's host cores, all threads and one thread; parity = normwise max
+    relative error between the two outputs on the same inputs.  The layer is
+    made with numpy (oracle/synthetic_np.py) so both sides read the same
+    bytes."""
+    import torch
+    import qwen_wlqfastshot_helen_beta_b200  # noqa: F401  (torch ops)
+    from qwen_wlqfastshot_helen_beta_b200 import _C
+    from oracle import synthetic_np as SN
+    N0, K0, M0 = 896, 4864, 8
+    L = SN.make_layer(N0, K0, group_size=GROUP, density=DENSITY, r=RANK, seed=2024)
+    d = dev
+    q = torch.from_numpy(L.q_packed).to(d)
+    lut = torch.from_numpy(L.lut_c).to(d)
+    off = torch.from_numpy(L.chunk_offsets).to(d)
+    cols16 = torch.from_numpy(L.chunk_cols).to(d)
+    vals8 = torch.from_numpy(L.chunk_vals).to(d)
+    lutp = _C.prepack_lut(lut, torch.float16)
+    colsp, deltap = _C.prepack_outliers(q, lut, off, cols16, vals8, N0, K0, 4, torch.float16, GROUP, 0)
+    A = torch.from_numpy(L.lora_A).to(d)
+    B = torch.from_numpy(L.lora_B).to(d)
+    gam = torch.from_numpy(L.dora_gamma).to(d)
+    rng = np.random.default_rng(4)
+    x_np = rng.standard_normal((M0, K0)).astype(np.float32)
+    x_host = torch.from_numpy(x_np).pin_memory()
+    y_host = torch.empty((M0, N0), dtype=torch.float32).pin_memory()
+    x_dev = x_host.to(d)
+    out16 = torch.empty((M0, N0), dtype=torch.float16, device=d)
+
+    def op(xd):
+        x16 = xd.to(torch.float16)
+        torch.ops.wlq_fastShot.gemm(x16, q, lutp, out16, N0, K0, 4, L.words_per_row, off, colsp, deltap, None, B,
+                                    gam, L.lora_scale, GROUP, 0, 1, A)
+        return out16.float()
+
+    for _ in range(5):
+        op(x_dev)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        op(x_dev)
+    e1.record()
+    torch.cuda.synchronize()
+    dev_ms = e0.elapsed_time(e1) / reps
+
+    def e2e_call():
+        y_host.copy_(op(x_host.to(d, non_blocking=True)), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(5):
+        e2e_call()
+    e0.record()
+    for _ in range(reps):
+        e2e_call()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / reps
+    y_gpu = y_host.numpy().copy()
+
+    # the reference's CPU steps on the same layer and activations
+    def cpu_ms(threads):
+        torch.set_num_threads(threads)
+        xt = torch.from_numpy(x_np)
+        times, y = [], None
+        t_start = time.perf_counter()
+        for i in range(200):
+            dt, _, y = _cpu_call(L, M0, None, xt)
+            if i >= 3:
+                times.append(dt)
+            if i >= 23 and time.perf_counter() - t_start > budget_s / 2:
+                break
+        return statistics.median(times) * 1e3, len(times), y
+
+    cores = os.cpu_count() or 1
+    cpu_all_ms, n_all, y_cpu = cpu_ms(cores)
+    cpu_one_ms, n_one, _ = cpu_ms(1)
+    torch.set_num_threads(cores)
+    y_cpu = y_cpu.numpy()
+    err = float(np.max(np.abs(y_gpu - y_cpu)) / max(1e-30, float(np.max(np.abs(y_cpu)))))
+    try:
+        cpu_model = next(l.split(":", 1)[1].strip() for l in open("/proc/cpuinfo") if l.startswith("model name"))
+    except Exception:
+        cpu_model = "unknown"
+    return {
+        "workload": "BASELINE config 0: one 4864 -> 896 layer (Qwen2.5-0.5B down_proj shape), M=8 fp32 "
+                    "activations ~N(0,1), group-128 codebooks, DoRA rank 16, 0.5% outliers",
+        "ours_ms_per_call": round(dev_ms, 4),
+        "ours_e2e_ms_per_call": round(e2e_ms, 4),
+        "ours_path": "x cast to fp16, torch.ops.wlq_fastShot.gemm(..., lora_A) (h = A x inside the GEMV), output "
+                     "cast to fp32, as WLQLinearMethod.apply runs it; e2e adds the pinned host->device copy of x "
+                     "and the device->host copy of y, host synchronised per call",
+        "reference_cpu_ms_per_call": round(cpu_all_ms, 3),
+        "reference_cpu_ms_per_call_1thread": round(cpu_one_ms, 3),
+        "cores": cores, "cpu_model": cpu_model,
+        "reference_cpu_path": "oracle/cpu_baseline.py: unpack -> gather -> outlier overwrite -> fp32 matmul -> "
+                              "DoRA epilogue (the reference's torch steps), h = F.linear(x, A) in fp32; median of "
+                              f"{n_all} (all threads) / {n_one} (1 thread) calls after 3 warm-up calls",
+        "speedup_e2e_vs_cpu": round(cpu_all_ms / e2e_ms, 1),
+        "max_rel_err_vs_cpu": err,
+        "tolerance": 5e-3,
+    }
+
+
+def reference_gpu_baseline(dev, peaks, reps=20):
+    """The reference's own CUDA kernels (compiled from its sources for
+    sm_100a into oracle/_ref by oracle/build_ref.sh) timed on this GPU beside
+    this package's path, on per-row codebooks (the only layout the
+    reference's kernels read), fp16 activations, config-1 and config-2 shapes.
+    Reference composition per call, as vllm_wlq/linear_method.py:937-1009 and
+    csrc/vllm_binding.cpp:253-419 run it: F.linear(x, A).float(), then
+    launch_gemv_chunk_csr (M = 1), launch_gemm_metalog_dora (2 <= M <= 15) or
+    launch_dequant_patch_metalog + torch.mm + launch_fused_dora_epilogue
+    (M >= 16).  Ours: torch.ops.wlq_fastShot.gemm(..., lora_A) on the
+    prepacked layer (one GEMV launch for M <= 16; wlq_lora_h + the tcgen05
+    GEMM above).  Each (linear, M) is a CUDA graph of `reps` calls over two
+    weight copies; a baseline leg, not part of the product path."""
+    import torch
+    path = os.path.join(ROOT, "oracle", "_ref", "libwlq_ref_kernels.so")
+    if not os.path.exists(path):
+        return {"unavailable": "oracle/_ref/libwlq_ref_kernels.so not built (needs the reference tree at build time)"}
+    import qwen_wlqfastshot_helen_beta_b200  # noqa: F401  (torch ops)
+    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+    ref = ctypes.CDLL(path)
+    ci, cf = ctypes.c_int, ctypes.c_float
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    copies = []
+    for c in range(2):
+        row = {}
+        for si, (name, K, N) in enumerate(SHAPES):
+            L = S.make_layer(N, K, group_size=0, density=DENSITY, r=RANK, seed=5000 + 31 * c + si, device=dev)
+            row[name] = L.prepack(torch.float16)
+        copies.append(row)
+    torch.cuda.synchronize()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    ws = torch.zeros(32 * max(N for _, _, N in SHAPES), dtype=torch.float32, device=dev)
+    Wd = torch.empty(max(N * K for _, K, N in SHAPES), dtype=torch.float16, device=dev)
+
+    def ref_call(L, x, out):
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        M, N, K = x.shape[0], L.N, L.K
+        nc = (K + 511) // 512
+        h = torch.nn.functional.linear(x, L.lora_A).float()
+        if M == 1:
+            ref.launch_gemv_chunk_csr(vp(L.q_packed), vp(L.lut_c), vp(x), vp(out), vp(ws), vp(L.chunk_offsets),
+                                      vp(L.chunk_cols), vp(L.chunk_vals), vp(L.lora_B), vp(h), vp(L.dora_gamma),
+                                      cf(L.lora_scale), ci(L.r), ci(N), ci(K), ci(4), ci(nc), st)
+        elif M < 16:
+            ref.launch_gemm_metalog_dora(vp(x), vp(L.q_packed), vp(L.lut_c), vp(out), vp(L.chunk_offsets),
+                                         vp(L.chunk_cols), vp(L.chunk_vals), vp(h), vp(L.lora_B), vp(L.dora_gamma),
+                                         cf(L.lora_scale), ci(L.r), ci(M), ci(N), ci(K), ci(4), ci(L.words_per_row),
+                                         ci(nc), ci(512), st)
+        else:
+            W = Wd[:N * K].view(N, K)
+            ref.launch_dequant_patch_metalog(vp(L.q_packed), vp(L.lut_c), vp(W), vp(L.chunk_offsets),
+                                             vp(L.chunk_cols), vp(L.chunk_vals), ci(N), ci(K), ci(4),
+                                             ci(L.words_per_row), ci(nc), ci(512), st)
+            torch.mm(x, W.t(), out=out)
+            ref.launch_fused_dora_epilogue(vp(out), vp(h), vp(L.lora_B), vp(L.dora_gamma), cf(L.lora_scale),
+                                           ci(L.r), ci(M), ci(N), st)
+
+    def our_call(L, x, out):
+        torch.ops.wlq_fastShot.gemm(x, L.q_packed, L.lut_packed, out, L.N, L.K, 4, L.words_per_row,
+                                    L.chunk_offsets, L.cols_packed, L.delta_packed, None, L.lora_B, L.dora_gamma,
+                                    L.lora_scale, 0, 0, 1, L.lora_A_act)
+
+    def time_graph(fn, name, x, out):
+        for c in range(2):
+            fn(copies[c][name], x, out)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(reps):
+                    fn(copies[i % 2][name], x, out)
+        torch.cuda.current_stream().wait_stream(s)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / reps
+
+    gemv, gemm = {}, {}
+    sums = {"gemv": [0.0, 0.0, 0.0], "gemm": [0.0, 0.0, 0.0]}  # ref ms, our ms, bytes or flops
+    for name, K, N in SHAPES:
+        for M in MS + GEMM_MS:
+            x = torch.randn((M, K), generator=gen, device=dev).to(torch.float16)
+            out_r = torch.empty((M, N), dtype=torch.float16, device=dev)
+            out_o = torch.empty((M, N), dtype=torch.float16, device=dev)
+            t_ref = time_graph(ref_call, name, x, out_r)
+            t_our = time_graph(our_call, name, x, out_o)
+            err = ((out_o.float() - out_r.float()).abs().max() / out_r.float().abs().max()).item()
+            key = f"{name}/M{M}"
+            if M <= 16:
+                b = copies[0][name].algorithmic_bytes(M)
+                gemv[key] = {"ref_us": round(t_ref * 1e3, 2), "ours_us": round(t_our * 1e3, 2),
+                             "ref_gbs": round(b / (t_ref * 1e-3) / 1e9, 1), "ours_gbs": round(b / (t_our * 1e-3) / 1e9, 1),
+                             "speedup": round(t_ref / t_our, 2), "max_rel_diff": round(err, 5)}
+                acc = sums["gemv"]
+                acc[2] += b
+            else:
+                fl = 2.0 * M * N * K
+                gemm[key] = {"ref_us": round(t_ref * 1e3, 1), "ours_us": round(t_our * 1e3, 1),
+                             "ref_tflops": round(fl / (t_ref * 1e-3) / 1e12, 1),
+                             "ours_tflops": round(fl / (t_our * 1e-3) / 1e12, 1),
+                             "speedup": round(t_ref / t_our, 2), "max_rel_diff": round(err, 5)}
+                acc = sums["gemm"]
+                acc[2] += fl
+            acc[0] += t_ref
+            acc[1] += t_our
+            del x, out_r, out_o
+    g_, m_ = sums["gemv"], sums["gemm"]
+    return {
+        "layout": "per-row fp16 codebooks (the reference's), rank 16, 0.5% outliers, fp16 activations, "
+                  "2 rotating weight copies",
+        "reference_kernels": "oracle/_ref/libwlq_ref_kernels.so (the reference's csrc/gemv_kernel.cu and "
+                             "csrc/gemm_kernel.cu built for sm_100a) + torch.mm (cuBLAS) + F.linear for h",
+        "gemv_vs_ref_gpu": round(g_[0] / g_[1], 2),
+        "gemv_ref_gbs": round(g_[2] / (g_[0] * 1e-3) / 1e9, 1),
+        "gemv_ours_gbs": round(g_[2] / (g_[1] * 1e-3) / 1e9, 1),
+        "gemm_vs_ref_gpu": round(m_[0] / m_[1], 2),
+        "gemm_ref_tflops": round(m_[2] / (m_[0] * 1e-3) / 1e12, 1),
+        "gemm_ours_tflops": round(m_[2] / (m_[1] * 1e-3) / 1e12, 1),
+        "per_config_gemv": gemv,
+        "per_config_gemm": gemm,
     }
 
 
 # ---------------------------------------------------------- CPU baseline
 
-def _cpu_sample_layers(seed=5):
-    """Row blocks (<= 512 rows, full K) of each linear, generated on the CPU."""
-    from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
+def _cpu_sample_layers(seed=5, rows=512):
+    """Row blocks (<= ``rows`` rows, full K) of each linear, generated with
+    numpy alone (oracle/synthetic_np.py): the CPU legs load no library of
+    this repository."""
+    from oracle import synthetic_np as SN
     out = []
     for si, (name, K, N) in enumerate(SHAPES):
-        rows = min(N, 512)
-        L = S.make_layer(rows, K, group_size=GROUP, density=DENSITY, r=RANK, seed=seed + si, device="cpu",
-                         row_block=128)
-        out.append((name, K, N, rows, L))
+        n = min(N, rows)
+        out.append((name, K, N, n, SN.make_layer(n, K, group_size=GROUP, density=DENSITY, r=RANK, seed=seed + si)))
     return out
 
 
-def _cpu_call(L, M, gen):
+def _cpu_operands(L):
+    """The layer's tensors as the reference's CPU steps take them (cached)."""
+    import torch
+    ops = getattr(L, "_cpu_ops", None)
+    if ops is None:
+        ops = (L.q_packed, torch.from_numpy(L.lut_c), L.chunk_offsets,
+               None if L.chunk_cols is None else L.chunk_cols.astype(np.int64), L.chunk_vals,
+               torch.from_numpy(L.lora_A).float(), torch.from_numpy(L.lora_B), torch.from_numpy(L.dora_gamma))
+        L._cpu_ops = ops
+    return ops
+
+
+def _cpu_call(L, M, gen, x=None):
+    """One forward through the reference's CPU steps: h = A x (the
+    reference's F.linear, vllm_wlq/linear_method.py:962-963), then
+    oracle/cpu_baseline.py.  Returns (seconds, algorithmic bytes, y)."""
     import torch
     from oracle.cpu_baseline import cpu_forward
-    x = torch.randn((M, L.K), generator=gen).to(torch.bfloat16)
+    q, lut, off, cols, vals, A, B, gam = _cpu_operands(L)
+    if x is None:
+        x = torch.randn((M, L.K), generator=gen).to(torch.bfloat16)
     t = time.perf_counter()
-    h = torch.nn.functional.linear(x.float(), L.lora_A.float())  # the reference's F.linear(x, A)
-    cpu_forward(L.q_packed.numpy(), L.words_per_row, L.lut_c, L.N, L.K, GROUP, 0, L.chunk_offsets.numpy(),
-                L.chunk_cols.numpy().astype(np.int64), L.chunk_vals.numpy(), x.float(), h, L.lora_B, L.dora_gamma,
-                L.lora_scale)
-    return time.perf_counter() - t, L.algorithmic_bytes(M)
+    h = torch.nn.functional.linear(x.float(), A)
+    y = cpu_forward(q, L.words_per_row, lut, L.N, L.K, L.group_size, L.group_offset, off, cols, vals, x.float(), h,
+                    B, gam, L.lora_scale)
+    return time.perf_counter() - t, L.algorithmic_bytes(M), y
 
 
 def cpu_baseline(budget_s=15.0):
@@ -600,7 +911,7 @@ def cpu_baseline(budget_s=15.0):
     while True:
         for (name, K, N, rows, L) in layers:
             for M in MS:
-                dt, b = _cpu_call(L, M, gen)
+                dt, b, _ = _cpu_call(L, M, gen)
                 tot_t += dt
                 tot_b += b
                 n += 1
@@ -609,8 +920,8 @@ def cpu_baseline(budget_s=15.0):
     return {"value": round(tot_b / tot_t / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
             "kind": "port",
             "sample": f"{n} calls: 512-row blocks (full K) of each of the 4 linears at M in {{1,4,8,16}}, "
-                      f"the reference's torch dequantize-then-matmul steps (oracle/cpu_baseline.py), "
-                      f"{tot_t:.1f} s of CPU time"}
+                      f"the reference's torch dequantize-then-matmul steps (oracle/cpu_baseline.py) on layers "
+                      f"made with numpy (oracle/synthetic_np.py), {tot_t:.1f} s of CPU time"}
 
 
 def run_reference(args):
@@ -627,7 +938,7 @@ def run_reference(args):
         _cpu_call(*cfgs[s % len(cfgs)], gen)
     tot_t = tot_b = 0.0
     for s in range(args.steps):
-        dt, b = _cpu_call(*cfgs[s % len(cfgs)], gen)
+        dt, b, _ = _cpu_call(*cfgs[s % len(cfgs)], gen)
         tot_t += dt
         tot_b += b
     value = tot_b / tot_t / 1e9
@@ -642,7 +953,8 @@ def run_reference(args):
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": "each step: one 512-row block (full K) of one linear at one M, cycling over "
                                    "the 4 linears x M in {1,4,8,16}; the reference's torch dequantize-then-"
-                                   "matmul steps (oracle/cpu_baseline.py)"},
+                                   "matmul steps (oracle/cpu_baseline.py) on layers made with numpy "
+                                   "(oracle/synthetic_np.py); no library of this repository is loaded"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -697,6 +1009,8 @@ def main():
     ap.add_argument("--copies", type=int, default=3)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-baselines", action="store_true", help="skip the config-0 CPU leg and the reference's GPU "
+                    "kernels leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

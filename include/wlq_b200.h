@@ -115,6 +115,15 @@ WLQ_API int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, 
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
              int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
 
+/* DoRA low-rank input H = X lora_A^T, fp32 [M, r], for the calls that do not
+ * compute it inside the decode GEMV (the prefill GEMM; rank above 48).  X
+ * [M, K] and lora_A [r, K] in act_dtype; tensor cores, fp32 accumulation, no
+ * workspace.  Replaces the library GEMM and cast before every reference GEMM
+ * op, F.linear(x, lora_A).float() (vllm_wlq/linear_method.py:984); H is not
+ * rounded to fp16 first. */
+WLQ_API int wlq_lora_h(const void* X, const void* lora_A, float* H, int M, int K, int r, int act_dtype,
+                       wlq_stream_t stream);
+
 /* Codebooks -> WLQ_LUT_PREPACKED layout for act_dtype: n_codebooks x 16 fp16
  * entries in, the same number of 32-byte records out (may not alias).  Done
  * once at load time; no reference counterpart (the reference converts per
@@ -186,6 +195,16 @@ WLQ_API int wlq_gemv_allreduce(const int32_t* q_packed, const void* lut_c, const
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
              int lut_group_offset, int lut_format, int act_dtype, void* const* tp_bufs, int tp_rank,
              int tp_world, int max_N, wlq_stream_t stream);
+
+/* Test and tuning hook of the decode GEMV's K split: wlq_gemv_set_split(cs)
+ * makes every later wlq_gemv / wlq_gemv_lora_a / wlq_gemm-as-GEMV launch of
+ * the process split K over a cluster of exactly cs CTAs (1..16, at most one
+ * per 128-column chunk; above 8 a non-portable cluster size the device must
+ * accept), 0 restores the per-call choice.  wlq_gemv_last_split() returns the
+ * split of the calling thread's last successful GEMV launch.  No reference
+ * counterpart (the reference's split-K is internal, csrc/gemv_kernel.cu:422-428). */
+WLQ_API int wlq_gemv_set_split(int cs);
+WLQ_API int wlq_gemv_last_split(void);
 
 /* Device error word of `device`: bit 0 (WLQ_DEVERR_WAIT_TIMEOUT) is set when
  * a pipeline wait inside a tensor-core GEMM kernel gave up (the kernel then

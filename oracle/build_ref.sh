@@ -9,8 +9,10 @@
 # the reference's csrc/vllm_binding.cpp needs libtorch and is not built.
 # Flags follow the reference's setup.py:20-34, with the arch set to sm_100a.
 set -euo pipefail
-REF=${1:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
+# the reference tree: the first argument, else WLQ_REFERENCE_TREE, else a
+# directory named "reference" beside this repository
+REF=${1:-${WLQ_REFERENCE_TREE:-$(dirname "$(cd "$HERE/.." && pwd -P)")/reference}}
 OUT="$HERE/_ref"
 mkdir -p "$OUT"
 if [ ! -f "$REF/csrc/gemv_kernel.cu" ]; then

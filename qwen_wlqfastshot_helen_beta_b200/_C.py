@@ -155,16 +155,39 @@ def gemv_forward(q_packed, lut_c, x, out, N, K, bits, chunk_offsets=None, chunk_
     check(rc, "wlq_gemv")
 
 
+def lora_h(x, lora_A, out=None):
+    """H = x lora_A^T in fp32 ([M, r]) on this package's tensor-core kernel
+    (wlq_lora_h): the DoRA low-rank input of the calls that do not compute it
+    inside the decode GEMV.  Replaces F.linear(x, lora_A).float()
+    (vllm_wlq/linear_method.py:962-963, 984); x [.., K] and lora_A [r, K] in
+    the same activation dtype."""
+    _check_common("lora_h", (x, lora_A), ("x", "lora_A"))
+    _require(lora_A.dim() == 2, "lora_h: lora_A must be [r, K]")
+    r, K = int(lora_A.shape[0]), int(lora_A.shape[1])
+    _require(lora_A.dtype == x.dtype, f"lora_h: lora_A dtype {lora_A.dtype} must match x dtype {x.dtype}")
+    _require(lora_A.device == x.device, f"lora_h: lora_A must be on {x.device}")
+    _require(K > 0 and x.numel() % K == 0, f"lora_h: x has {x.numel()} elements, not a multiple of K={K}")
+    M = x.numel() // K
+    if out is None:
+        out = torch.empty((M, r), dtype=torch.float32, device=x.device)
+    _require(out.is_cuda and out.is_contiguous() and out.dtype == torch.float32 and out.numel() == M * r,
+             f"lora_h: out must be a contiguous float32 CUDA tensor of {M}x{r} values")
+    with _DeviceGuard(x.device):
+        rc = lib.wlq_lora_h(_ptr(x), _ptr(lora_A), _ptr(out), M, K, r, _act_dtype(x), _stream(x.device))
+    check(rc, "wlq_lora_h")
+    return out
+
+
 _SM_COUNT = {}
 
 
 def folds_h(M, N, K, r, lut_format, x) -> bool:
     """Whether gemv_lora_a takes this call (the GEMV computing h = A x): up
-    to 16 tokens with r <= 32, or 17..32 tokens with r <= 16 when the
+    to 16 tokens with r <= 48, or 17..32 tokens with r <= 16 when the
     tensor-core GEMM's 128-row tiles would not fill the device (the rule
     wlq_gemm applies, csrc/wlq_abi.cu gemv_preferred); prepacked layout and
     16-byte aligned rows either way."""
-    if not (0 < r <= 32 and lut_format == WLQ_LUT_PREPACKED and K % 8 == 0 and x.data_ptr() % 16 == 0):
+    if not (0 < r <= 48 and lut_format == WLQ_LUT_PREPACKED and K % 8 == 0 and x.data_ptr() % 16 == 0):
         return False
     if M <= 16:
         return True
@@ -179,7 +202,7 @@ def folds_h(M, N, K, r, lut_format, x) -> bool:
 def gemv_lora_a(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B, lora_A,
                 dora_gamma, lora_scale=1.0, lut_group_size=0, lut_group_offset=0, lut_format=WLQ_LUT_PREPACKED):
     """Decode GEMV (M <= 32) that computes the DoRA input h = lora_A x itself
-    (lora_A [r, K] in x's dtype, r <= 32, r <= 16 above 16 tokens; prepacked
+    (lora_A [r, K] in x's dtype, r <= 48, r <= 16 above 16 tokens; prepacked
     layout): one launch in place of F.linear + .float() + GEMV
     (vllm_wlq/linear_method.py:962-999)."""
     N, K, bits = int(N), int(K), int(bits)

@@ -42,10 +42,12 @@ def _register_ops():
         lut_format: int = 0,
         lora_A: Optional[torch.Tensor] = None,
     ) -> None:
-        if lora_A is not None and lora_h is None:  # h = A x inside the GEMV
-            _C.gemv_lora_a(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
-                           lora_A, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
-            return
+        if lora_A is not None and lora_h is None:
+            if _C.folds_h(1, int(N), int(K), int(lora_A.shape[0]), lut_format, x):  # h = A x inside the GEMV
+                _C.gemv_lora_a(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
+                               lora_A, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
+                return
+            lora_h = _C.lora_h(x.reshape(1, int(K)), lora_A)  # this package's own kernel, before the GEMV
         _C.gemv_forward(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
                         lora_h, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
 
@@ -83,8 +85,8 @@ def _register_ops():
                 _C.gemv_lora_a(q_packed, lut_c, X, out, N, K, bits, chunk_offsets, chunk_cols, chunk_vals, lora_B,
                                lora_A, dora_gamma, lora_scale, lut_group_size, lut_group_offset, lut_format)
                 return
-            # otherwise h = A x as one library GEMM, as the reference computes it
-            lora_H = torch.nn.functional.linear(X.reshape(M, int(K)), lora_A).float()
+            # otherwise H = X A^T on this package's own kernel, before the GEMM
+            lora_H = _C.lora_h(X.reshape(M, int(K)), lora_A)
         _C.gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets, chunk_cols,
                         chunk_vals, lora_H, lora_B, dora_gamma, lora_scale, lut_group_size, lut_group_offset,
                         lut_format)

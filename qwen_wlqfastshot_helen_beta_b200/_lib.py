@@ -31,6 +31,7 @@ SIGNATURES = {
                                _i32, _i32, _i32, _i32, _p]),
     "wlq_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
                         _i32, _i32, _i32, _i32, _p]),
+    "wlq_lora_h": (_i32, [_p, _p, _p, _i32, _i32, _i32, _i32, _p]),
     "wlq_prepack_lut": (_i32, [_p, _p, _i64, _i32, _p]),
     "wlq_prepack_lut_host": (_i32, [_p, _p, _i64, _i32]),
     "wlq_prepack_outliers": (_i32, [_p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p,
@@ -38,6 +39,8 @@ SIGNATURES = {
     "wlq_dequant": (_i32, [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p]),
     "wlq_init_workspaces": (_i32, [_i64, _i64, _i32]),
     "wlq_device_error": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint), _i32]),
+    "wlq_gemv_set_split": (_i32, [_i32]),
+    "wlq_gemv_last_split": (_i32, []),
     "wlq_tp_buffer_bytes": (ctypes.c_size_t, [_i32, _i32]),
     "wlq_tp_buffer_alloc": (_i32, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
     "wlq_tp_buffer_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),

@@ -190,6 +190,22 @@ int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* ou
     return launch_gemm(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int wlq_lora_h(const void* X, const void* lora_A, float* H, int M, int K, int r, int act_dtype,
+               wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    if (M < 0 || K < 0 || r < 0) return fail(WLQ_ERR_INVALID_ARG, "wlq_lora_h: negative size (M=%d K=%d r=%d)", M, K, r);
+    if (act_dtype != WLQ_DTYPE_F16 && act_dtype != WLQ_DTYPE_BF16)
+        return fail(WLQ_ERR_UNSUPPORTED, "wlq_lora_h: act_dtype must be WLQ_DTYPE_F16 or WLQ_DTYPE_BF16 (got %d)",
+                    act_dtype);
+    if (M == 0 || r == 0) return WLQ_OK;
+    if (!X || !lora_A || !H) return fail(WLQ_ERR_INVALID_ARG, "wlq_lora_h: X, lora_A and H are required");
+    if (!aligned(X, 2) || !aligned(lora_A, 2) || !aligned(H, 4))
+        return fail(WLQ_ERR_ALIGNMENT, "wlq_lora_h: misaligned pointer");
+    int rc = require_sm100();
+    if (rc) return rc;
+    return launch_lora_h(X, lora_A, H, M, K, r, act_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int wlq_dequant(const int32_t* q_packed, const void* lut_c, void* W_out, const int32_t* chunk_offsets,
                 const uint16_t* chunk_cols, const uint8_t* chunk_vals, int N, int K, int bits, int words_per_row,
                 int lut_group_size, int lut_group_offset, wlq_stream_t stream) {

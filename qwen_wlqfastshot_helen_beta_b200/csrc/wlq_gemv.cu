@@ -33,6 +33,7 @@
 // its tile (the arithmetic of csrc/gemv_kernel.cu:262-288): two lanes per row
 // walk the row's chunk-CSR entries, accumulate in registers and combine with
 // one shuffle.
+#include <atomic>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -113,6 +114,9 @@ struct FitKey {
 
 namespace gemv {
 
+std::atomic<int> g_forced_split{0};
+thread_local int g_last_split = 0;
+
 int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit) {
     static std::mutex mu;
     static std::vector<std::pair<FitKey, int>> cache;
@@ -129,7 +133,13 @@ int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit)
         }
     int n = 0;
     e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-    if (e != cudaSuccess) return check_cuda(e, "cudaOccupancyMaxActiveClusters");
+    if (e != cudaSuccess) {
+        // a cluster size the device or driver does not run: none fits; the
+        // refusal is cached, so the query runs once per shape
+        if (key.cy <= 8 || !cluster_size_refused(e)) return check_cuda(e, "cudaOccupancyMaxActiveClusters");
+        cudaGetLastError();  // clears this call's (non-sticky) error only
+        n = 0;
+    }
     cache.emplace_back(key, n);
     *fit = n;
     return WLQ_OK;
@@ -176,9 +186,9 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     }
     const bool xvec = (a.K % 8 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
     // h = A x in the kernel: r <= 16 rt
-    const int rt = a.loraA != nullptr && a.r > 0 ? (a.r <= 16 ? 1 : 2) : 0;
+    const int rt = a.loraA != nullptr && a.r > 0 ? (a.r + 15) / 16 : 0;
     if (rt > 0) {
-        if (a.r > 32) return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: h = A x in the kernel needs r <= 32 (r=%d)", a.r);
+        if (a.r > 48) return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: h = A x in the kernel needs r <= 48 (r=%d)", a.r);
         if (a.M > 16 && a.r > 16)
             return fail(WLQ_ERR_UNSUPPORTED, "wlq_gemv: h = A x in the kernel for more than 16 tokens needs r <= 16");
         if (!a.lut_prepacked)
@@ -191,7 +201,10 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     const int tiles = (a.N + kRowsPerTile - 1) / kRowsPerTile;
     const int ctas = (tiles + kWarps - 1) / kWarps;
     const int slots = codebook_slots(p.G);
-    const int ring_bytes = kWarps * kStages * ring_stage_bytes(slots, rt);
+    // r <= 48 (rt = 3) always runs a 2-stage ring: three stages of its larger
+    // A blocks would leave no room for 4 CTAs per SM
+    const int stages = rt == 3 ? 2 : kStages;
+    const int ring_bytes = kWarps * stages * ring_stage_bytes(slots, rt);
 
     auto configure = [&](int cs) {
         Plan pl;
@@ -204,8 +217,9 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
         // that lets the activations be staged.
         const int64_t x_bytes = ((int64_t)a.M * p.x_stride * 2 + 127) / 128 * 128;
         pl.xsmem = x_bytes + ring_bytes <= 48 * 1024;
-        pl.stages2 = rt > 0 && a.M > 8 && !pl.xsmem && x_bytes + ring_bytes / kStages * 2 <= 48 * 1024;
-        pl.xsmem = pl.xsmem || pl.stages2;
+        pl.stages2 = rt == 3 ||
+                     (rt > 0 && a.M > 8 && !pl.xsmem && x_bytes + ring_bytes / kStages * 2 <= 48 * 1024);
+        if (rt != 3) pl.xsmem = pl.xsmem || pl.stages2;
         p.x_bytes = pl.xsmem ? (int)x_bytes : 0;
         return pl;
     };
@@ -219,28 +233,58 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     // per SM are in flight, keeping at least 2 chunks per rank, and at least 4
     // above 8 ranks (measured: a 14-way split of 28 chunks lost to the wider
     // reduction, a 16-way split of 148 won 15 %); then take the largest split
-    // (down to none) whose clusters the device holds in one wave.
-    const int sms = device_sm_count();
-    auto chunks_ok = [&](int cs) { return p.kchunks >= (cs > 8 ? 4 : 2) * cs; };
-    int cs_max = 1;
-    while (cs_max < kMaxSplit && (int64_t)ctas * cs_max < 4LL * sms && chunks_ok(cs_max + 1)) ++cs_max;
+    // (down to none) whose clusters the device holds in one wave.  A split
+    // forced through wlq_gemv_set_split replaces the choice.
+    const int forced = g_forced_split.load(std::memory_order_relaxed);
     Plan pl = configure(1);
-    for (int cs = cs_max; cs > 1; --cs) {
-        const Plan c = configure(cs);
-        int fit = 0;
-        const int rc = run(c, &fit);
-        if (rc && cs > 8) {  // a non-portable cluster size the device or driver refused: try smaller
-            cudaGetLastError();
-            continue;
-        }
-        if (rc) return rc;
-        if (ctas <= fit) {
-            pl = c;
-            break;
+    if (forced > 0) {
+        if (forced > kMaxSplit || forced > p.kchunks)
+            return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: forced split %d needs 1..%d and at most %d chunks of 128 "
+                        "columns", forced, kMaxSplit, p.kchunks);
+        pl = configure(forced);
+    } else {
+        const int sms = device_sm_count();
+        auto chunks_ok = [&](int cs) { return p.kchunks >= (cs > 8 ? 4 : 2) * cs; };
+        int cs_max = 1;
+        while (cs_max < kMaxSplit && (int64_t)ctas * cs_max < 4LL * sms && chunks_ok(cs_max + 1)) ++cs_max;
+        for (int cs = cs_max; cs > 1; --cs) {
+            const Plan c = configure(cs);
+            int fit = 0;
+            const int rc = run(c, &fit);  // a refused non-portable size reports fit = 0 (cached)
+            if (rc) return rc;
+            if (ctas <= fit) {
+                pl = c;
+                break;
+            }
         }
     }
     configure(pl.cs);
-    return run(pl, nullptr);
+    int rc = run(pl, nullptr);
+    if (rc == kRetryPortable && forced == 0) {
+        // the launch refused a non-portable cluster size: once more at 8 CTAs
+        // or fewer
+        int cs = pl.cs > 8 ? 8 : pl.cs;
+        while (cs > 1 && p.kchunks < 2 * cs) --cs;
+        pl = configure(cs);
+        rc = run(pl, nullptr);
+    }
+    if (rc == kRetryPortable)
+        return fail(WLQ_ERR_CUDA, "wlq_gemv: the device refused a cluster of %d CTAs", pl.cs);
+    if (rc == WLQ_OK) g_last_split = pl.cs;
+    return rc;
 }
 
 }  // namespace wlq
+
+extern "C" {
+
+int wlq_gemv_set_split(int cs) {
+    if (cs < 0 || cs > wlq::gemv::kMaxSplit)
+        return wlq::fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_set_split: %d is outside 0..%d", cs, wlq::gemv::kMaxSplit);
+    wlq::gemv::g_forced_split.store(cs, std::memory_order_relaxed);
+    return WLQ_OK;
+}
+
+int wlq_gemv_last_split(void) { return wlq::gemv::g_last_split; }
+
+}  // extern "C"

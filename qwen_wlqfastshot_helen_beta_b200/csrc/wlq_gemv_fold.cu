@@ -1,5 +1,6 @@
 // Instantiations of the decode GEMV that computes the DoRA low-rank input
-// h = A x itself (RT = 1 for r <= 16, 2 for r <= 32): the F.linear(x, A) and
+// h = A x itself (RT = 1 for r <= 16, 2 for r <= 32, 3 for r <= 48): the
+// F.linear(x, A) and
 // .float() launches that precede every reference GEMV
 // (vllm_wlq/linear_method.py:962-963) folded into the one kernel.  Prepacked
 // codebooks and outliers and 16-byte aligned rows only, as the load path
@@ -15,6 +16,9 @@ namespace {
 template <typename T, int NT, int NSLOT>
 int fold_x(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int cs, cudaStream_t stream,
            int* fit) {
+    if (rt == 3)  // r <= 48 (a fused qkv of three rank-16 adapters): always a 2-stage ring
+        return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 3, 2>(p, ctas, cs, stream, fit)
+                     : launch_variant<T, NT, NSLOT, true, true, false, 3, 2>(p, ctas, cs, stream, fit);
     if constexpr (NT == 2) {
         if (stages2 && xsmem)  // 16 tokens staged beside a 2-stage ring
             return rt == 1 ? launch_variant<T, NT, NSLOT, true, true, true, 1, 2>(p, ctas, cs, stream, fit)

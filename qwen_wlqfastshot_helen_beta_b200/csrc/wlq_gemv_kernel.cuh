@@ -2,6 +2,8 @@
 // wlq_gemv.cu (low-rank input h given) and wlq_gemv_fold.cu (h = A x computed
 // in the kernel); the design notes are at the top of wlq_gemv.cu.
 #pragma once
+#include <atomic>
+
 #include "wlq_common.cuh"
 #include "wlq_internal.h"
 
@@ -80,17 +82,23 @@ __device__ __forceinline__ void stage_x_issue(uint16_t* xs, const T* __restrict_
 
 // Sum over the cluster's ranks of one partial-tile element, rank 0 first:
 // the remote loads are all issued before the adds.
-__device__ __forceinline__ float cluster_sum(const float* own, uint32_t nranks) {
-    if (nranks == 1) return *own;
-    const uint32_t a = smem_u32(own);
-    float v[kMaxSplit];
+template <int MAXR>
+__device__ __forceinline__ float cluster_sum_n(uint32_t a, uint32_t nranks) {
+    float v[MAXR];
 #pragma unroll
-    for (int q = 0; q < kMaxSplit; ++q)
+    for (int q = 0; q < MAXR; ++q)
         v[q] = (uint32_t)q < nranks ? ld_shared_cluster_f32(mapa_shared(a, (uint32_t)q)) : 0.f;
     float s = v[0];
 #pragma unroll
-    for (int q = 1; q < kMaxSplit; ++q) s += v[q];
+    for (int q = 1; q < MAXR; ++q) s += v[q];
     return s;
+}
+__device__ __forceinline__ float cluster_sum(const float* own, uint32_t nranks) {
+    if (nranks == 1) return *own;
+    const uint32_t a = smem_u32(own);
+    // the portable sizes (<= 8) keep to 8 loads in flight; adding zeros past
+    // nranks leaves the sum unchanged
+    return nranks <= 8 ? cluster_sum_n<8>(a, nranks) : cluster_sum_n<kMaxSplit>(a, nranks);
 }
 
 // Per-warp shared-memory ring of S stages, filled by cp.async (no register
@@ -661,8 +669,25 @@ inline int codebook_slots(int G) { return G == 0 ? 0 : G >= kChunk ? 2 : 4; }
 inline int ring_stage_bytes(int slots, int rt) { return kRowsPerTile * 64 + kRowsPerTile * slots * 32 + rt * 16 * 64; }
 
 // Clusters of the launch shape `cfg` that the device holds at once (cached
-// per kernel, shape and shared memory size).
+// per kernel, shape and shared memory size; 0 for a non-portable size the
+// device refuses).
 int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit);
+
+// Split forced by wlq_gemv_set_split (0 = chosen per call) and the split of
+// this thread's last launch (wlq_gemv_last_split).
+extern std::atomic<int> g_forced_split;
+extern thread_local int g_last_split;
+
+// Returned by a launch whose non-portable cluster size (> 8) the device
+// refused (the error is cleared): the caller retries at 8 CTAs or fewer.
+constexpr int kRetryPortable = -1;
+
+// The errors with which the runtime refuses a cluster size above the portable
+// 8 CTAs (as opposed to a failure of the call itself).
+inline bool cluster_size_refused(cudaError_t e) {
+    return e == cudaErrorInvalidClusterSize || e == cudaErrorLaunchOutOfResources ||
+           e == cudaErrorInvalidValue || e == cudaErrorNotSupported;
+}
 
 // Launches one variant; with `fit` set, reports instead how many of its
 // clusters the device holds at once (INT_MAX when it runs without clusters).
@@ -681,7 +706,15 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, i
     }
     if (cs > 8) {  // clusters above the portable size of 8
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return check_cuda(e, "gemv_kernel cluster size attribute");
+        if (e != cudaSuccess) {
+            if (!cluster_size_refused(e)) return check_cuda(e, "gemv_kernel cluster size attribute");
+            cudaGetLastError();
+            if (fit) {
+                *fit = 0;
+                return WLQ_OK;
+            }
+            return kRetryPortable;
+        }
     }
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -699,7 +732,12 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, i
         }
         return clusters_that_fit(reinterpret_cast<const void*>(kern), cfg, fit);
     }
-    return check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "gemv_kernel launch");
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess && cs > 8 && cluster_size_refused(e)) {
+        cudaGetLastError();
+        return kRetryPortable;
+    }
+    return check_cuda(e, "gemv_kernel launch");
 }
 
 // Launches the kernel that computes h = A x itself (p.loraA, r <= 16 rt,

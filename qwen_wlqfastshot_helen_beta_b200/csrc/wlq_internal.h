@@ -63,6 +63,7 @@ constexpr TpLayout tp_layout(int world, int max_N) {
 
 int launch_gemv(const LinearArgs& a, cudaStream_t stream);
 int launch_gemm(const LinearArgs& a, cudaStream_t stream);
+int launch_lora_h(const void* X, const void* A, float* H, int M, int K, int r, int dtype, cudaStream_t stream);
 int launch_prepack_outliers(const uint32_t* q, const uint16_t* lut, const int32_t* off, const uint16_t* ccols,
                             const uint8_t* cvals, int N, int K, int wpr, int group_size, int goff, int ngroups,
                             int chunk_m, int ncsr, int dtype, uint32_t* recs, float* delta, cudaStream_t stream);

@@ -485,7 +485,7 @@ class WLQLinearMethod(LinearMethodBase):
             if A.data_ptr() % 16 == 0 and _C.folds_h(M, layer.N, layer.K, int(lora_B.shape[1]), fmt, x2):
                 lora_A = A
             else:
-                lora_h = F.linear(x2, A).float()
+                lora_h = _C.lora_h(x2, A)
         if M == 1:
             torch.ops.wlq_fastShot.gemv(layer.q_packed_aligned, lut, x2.squeeze(0), out.squeeze(0), layer.N,
                                         layer.K, bits, layer.chunk_offsets, cols, vals,

@@ -292,8 +292,15 @@ def layer_vectors(lm, rng, tmpdir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None, help="reference source tree (default: WLQ_REFERENCE_TREE, else a "
+                    "'reference' directory beside this repository)")
     args = ap.parse_args()
+    if args.ref is None:
+        sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+        from oracle.reference_tree import locate
+        args.ref = locate()
+        if args.ref is None:
+            sys.exit("reference tree not found: pass --ref or set WLQ_REFERENCE_TREE")
     lm = load_reference(args.ref)
     rng = np.random.default_rng(20261201)
     codecs = codec_vectors(lm, rng)

@@ -101,6 +101,8 @@ FOLD_CASES = [
     (1200, 512, 128, 0, 16),   # many row tiles, no cluster
     (4100, 384, 128, 0, 16),   # no K split, ragged last CTA
     (18944, 1024, 128, 0, 32), # no K split, rank in two MMA tiles
+    (256, 3584, 128, 0, 48),   # rank in three MMA tiles (a fused qkv of three rank-16 adapters), 2-stage ring
+    (100, 1024, 0, 0, 40),     # per-row codebooks, rank 40 padded to three tiles
 ]
 
 
@@ -117,7 +119,7 @@ def test_gemv_lora_a_matches_oracle(case, dtype):
     cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], L.N, L.K, 4, dtype, L.G,
                                       L.goff)
     A = T["A"].to(dtype).contiguous()
-    for M in (1, 2, 5, 8, 9, 16) + ((17, 32) if r <= 16 else ()):
+    for M in (1, 2, 5, 8, 9, 16) + ((17, 32) if r <= 16 else ()):  # r > 16 above 16 tokens: see folds_h
         x, h = inputs(rng, L, M, dtype)
         ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
         y = torch.full((M, N), float("nan"), dtype=dtype, device="cuda")
@@ -133,21 +135,77 @@ def test_gemv_lora_a_matches_oracle(case, dtype):
 
 
 def test_gemv_lora_a_rejects():
-    """The in-kernel h needs the prepacked layout, r <= 32 and 16-byte rows."""
+    """The in-kernel h needs the prepacked layout, r <= 48 and 16-byte rows."""
     rng = np.random.default_rng(3)
-    L = make_np_layer(rng, 32, 256, 0, 0, r=48)
+    L = make_np_layer(rng, 32, 256, 0, 0, r=56)
     T = dev_layer(L)
     x = torch.randn((2, 256), device="cuda", dtype=torch.float16)
     y = torch.empty((2, 32), device="cuda", dtype=torch.float16)
     lut = C().prepack_lut(T["lut"], torch.float16)
     cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], 32, 256, 4, torch.float16)
-    with pytest.raises(RuntimeError, match="r <= 32"):
+    with pytest.raises(RuntimeError, match="r <= 48"):
         C().gemv_lora_a(T["q"], lut, x, y, 32, 256, 4, T["off"], cols, vals, T["B"], T["A"], T["gamma"], 1.0)
     L = make_np_layer(rng, 32, 256, 0, 0, r=16)
     T = dev_layer(L)
     with pytest.raises(RuntimeError, match="prepacked"):
         C().gemv_lora_a(T["q"], T["lut"], x, y, 32, 256, 4, T["off"], T["cols"], T["vals"], T["B"], T["A"],
                         T["gamma"], 1.0, lut_format=0)
+
+
+@pytest.mark.parametrize("split", [11, 13, 16])
+def test_gemv_forced_split_matches_oracle(split):
+    """K split over non-portable clusters (more than 8 CTAs, not a power of
+    two) forced through wlq_gemv_set_split: the cluster reduction of 11, 13
+    or 16 partial tiles against the oracle, h given and h computed in the
+    kernel, and wlq_gemv_last_split reporting the split that ran."""
+    from qwen_wlqfastshot_helen_beta_b200 import _lib
+    lib = _lib.lib
+    rng = np.random.default_rng(split)
+    N, K = 160, 18944  # 148 chunks of 128 columns
+    L = make_np_layer(rng, N, K, 128, 0, density=0.01, r=16)
+    T = dev_layer(L)
+    dtype = torch.bfloat16
+    lut = C().prepack_lut(T["lut"], dtype)
+    cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], N, K, 4, dtype, 128, 0)
+    A = T["A"].to(dtype).contiguous()
+    _lib.check(lib.wlq_gemv_set_split(split), "wlq_gemv_set_split")
+    try:
+        for M in (1, 8, 16):
+            x, h = inputs(rng, L, M, dtype)
+            ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+            y = torch.full((M, N), float("nan"), dtype=dtype, device="cuda")
+            C().gemv_lora_a(T["q"], lut, x, y, N, K, 4, T["off"], cols, vals, T["B"], A, T["gamma"], L.scale, 128, 0)
+            torch.cuda.synchronize()
+            assert lib.wlq_gemv_last_split() == split
+            assert rel_err(y.float().cpu().numpy(), ref) <= TOL[dtype], (M, "h in the kernel")
+            y2 = run_ours(L, T, x, h, gemv=(M == 1), fmt=1)
+            assert lib.wlq_gemv_last_split() == split
+            assert rel_err(y2.float().cpu().numpy(), ref) <= TOL[dtype], (M, "h given")
+    finally:
+        _lib.check(lib.wlq_gemv_set_split(0), "wlq_gemv_set_split")
+    with pytest.raises(RuntimeError, match="outside"):
+        _lib.check(lib.wlq_gemv_set_split(17), "wlq_gemv_set_split")
+
+
+@pytest.mark.parametrize("M,K,r", [(1, 3584, 16), (7, 1000, 48), (64, 3584, 64), (200, 4864, 48), (512, 18944, 16),
+                                   (2048, 3584, 80), (8192, 3584, 48), (33, 1004, 16), (130, 3586, 24)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_lora_h_matches_fp32(M, K, r, dtype):
+    """wlq_lora_h (H = X A^T on the tensor core, fp32 accumulation; K split
+    over a cluster for few token tiles, ranks past 64 in a second grid plane,
+    unaligned rows on the row kernel) against the same product in fp32."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(M * 7 + K + r)
+    X = torch.randn((M, K), generator=g, device="cuda").to(dtype)
+    A = (torch.randn((r, K), generator=g, device="cuda") * 0.01).to(dtype)
+    H = C().lora_h(X, A)
+    torch.cuda.synchronize()
+    ref = X.double() @ A.double().t()
+    err = ((H.double() - ref).abs().max() / ref.abs().max()).item()
+    assert H.shape == (M, r) and H.dtype == torch.float32
+    assert err <= 1e-5, err
+    H2 = C().lora_h(X, A)  # the cluster reduction sums in rank order: the same bits every call
+    assert torch.equal(H, H2)
 
 
 def test_gemv_outlier_edges():
@@ -187,15 +245,11 @@ def _p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
-@pytest.mark.parametrize("N,K", [(256, 1024), (96, 3584), (40, 512)])
-def test_against_reference_kernels(N, K):
-    """Same inputs through launch_gemv_chunk_csr (M=1), launch_gemm_metalog_dora
-    (2<=M<=15) and dequant + cuBLAS + epilogue (M>=16), the reference's three
-    paths (csrc/vllm_binding.cpp:253-419); fp16, per-row codebooks."""
-    lib = _ref_lib()
-    rng = np.random.default_rng(N * K)
-    L = make_np_layer(rng, N, K, 0, 0, density=0.01, outliers=True, dora=True)
+def _compare_with_reference_kernels(lib, L, Ms, rng, tol=5e-3):
+    """Same inputs through the reference's own CUDA kernels and ours, both
+    against the oracle (fp16 activations, as the reference casts them)."""
     T = dev_layer(L)
+    N, K = L.N, L.K
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     nc = (K + 511) // 512
     i, f = ctypes.c_int, ctypes.c_float
@@ -207,8 +261,10 @@ def test_against_reference_kernels(N, K):
     C().dequant_w0(T["q"], T["lut"], Wm, N, K, 4, L.wpr, T["off"], T["cols"], T["vals"])
     torch.cuda.synchronize()
     assert torch.equal(Wr.view(torch.int16), Wm.view(torch.int16))
+    del Wm
     ws = torch.zeros(32 * N, dtype=torch.float32, device="cuda")
-    for M in (1, 4, 15, 16, 32):
+    W = L.dense()
+    for M in Ms:
         x, h = inputs(rng, L, M, torch.float16)
         ref = torch.empty((M, N), dtype=torch.float16, device="cuda")
         if M == 1:
@@ -225,11 +281,34 @@ def test_against_reference_kernels(N, K):
                                            stream)
         torch.cuda.synchronize()
         y = run_ours(L, T, x, h, gemv=(M == 1))
-        oracle = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+        oracle = O.forward_f64(W, x.float().cpu().numpy(), h.cpu().numpy(), L.B, L.gamma, L.scale)
         e_ours = rel_err(y.float().cpu().numpy(), oracle)
         e_ref = rel_err(ref.float().cpu().numpy(), oracle)
         e_pair = rel_err(y.float().cpu().numpy(), ref.float().cpu().numpy())
-        assert e_ours <= 5e-3 and e_ref <= 5e-3 and e_pair <= 5e-3, (M, e_ours, e_ref, e_pair)
+        assert e_ours <= tol and e_ref <= tol and e_pair <= tol, (M, e_ours, e_ref, e_pair)
+
+
+@pytest.mark.parametrize("N,K", [(256, 1024), (96, 3584), (40, 512)])
+def test_against_reference_kernels(N, K):
+    """Same inputs through launch_gemv_chunk_csr (M=1), launch_gemm_metalog_dora
+    (2<=M<=15) and dequant + cuBLAS + epilogue (M>=16), the reference's three
+    paths (csrc/vllm_binding.cpp:253-419); fp16, per-row codebooks."""
+    lib = _ref_lib()
+    rng = np.random.default_rng(N * K)
+    L = make_np_layer(rng, N, K, 0, 0, density=0.01, outliers=True, dora=True)
+    _compare_with_reference_kernels(lib, L, (1, 4, 15, 16, 32), rng)
+
+
+@pytest.mark.parametrize("name,K,N", [("qkv", 3584, 4608), ("o", 3584, 3584), ("gate_up", 3584, 37888),
+                                      ("down", 18944, 3584)])
+def test_against_reference_kernels_config1(name, K, N):
+    """The BASELINE config-1 shapes at full size with per-row codebooks (the
+    reference's layout), 0.5% outliers and rank 16: the reference's three
+    kernel paths and ours against the oracle at M in {1, 4, 8, 16}."""
+    lib = _ref_lib()
+    rng = np.random.default_rng(K + N)
+    L = make_np_layer(rng, N, K, 0, 0, density=0.005, outliers=True, dora=True)
+    _compare_with_reference_kernels(lib, L, (1, 4, 8, 16), rng)
 
 
 # ------------------------------------------------------------- full sizes

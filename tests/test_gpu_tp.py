@@ -1,18 +1,27 @@
-"""Fused row-parallel all-reduce (wlq_gemv_allreduce) on 2 GPUs: each rank's
-K shard through the GEMV with the sum over ranks done in the kernel over
-NVLink peer memory, against the ranks' own outputs summed after an NCCL
-all-gather.  Eager calls (h given, or h = A x of the rank's columns of A
-computed in the kernel) and CUDA-graph replays (the per-tile epochs advance
-on the device), several token counts.  Skipped with fewer than 2 GPUs."""
+"""Fused row-parallel all-reduce (wlq_gemv_allreduce) across 2, 4 and 8 GPUs
+(each size runs when that many GPUs are present): every rank takes its K
+shard of one layer -- cut the way vLLM's row-parallel layers shard K,
+codebook groups carried with their offset -- through the GEMV with the sum
+over ranks done inside the kernel over NVLink peer memory.  The ranks'
+outputs must be identical bit for bit, and match the oracle's float64 forward
+of the UNSHARDED layer.  Eager calls (h given, and h = A x of the rank's
+columns computed in the kernel), a down-proj shard with a forced 11-CTA K
+split feeding the exchange, and CUDA-graph replays (the per-tile epochs
+advance on the device)."""
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
+
+from _layers import make_np_parts, rel_err
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+TOL = 2e-2  # bf16 activations, normwise max relative error
 
 
 def _free_port():
@@ -23,93 +32,102 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, port, results):
+# (name, N, K, tokens, forced K split of each rank's GEMV or 0)
+CASES = [("o", 512, 3584, (1, 5, 16), 0), ("down", 256, 18944, (1, 16), 11)]
+
+
+def _inputs(seed, K, M):
+    rng = np.random.default_rng(seed)
+    return torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16)
+
+
+def _rank_main(rank, world, port, results):
     import sys
+    import ctypes
     sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
     from datetime import timedelta
     import torch.distributed as dist
-    from qwen_wlqfastshot_helen_beta_b200 import _C, synthetic as S
+    from _gpu import dev_layer
+    from qwen_wlqfastshot_helen_beta_b200 import _C, _lib
     from qwen_wlqfastshot_helen_beta_b200.tp import TPComm
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=60), device_id=dev)
     comm = None
+    out = {}
     try:
-        N, Kp = 3584, 1792  # row-parallel shard of a 3584-wide K
-        L = S.make_layer(N, Kp, group_size=128, density=0.005, r=16, seed=40 + rank, device=dev)
-        L.prepack(torch.bfloat16)
-        comm = TPComm(max_N=N)
-        lut, cols, vals, fmt = L.operands_for(torch.bfloat16)
-        errs = []
-        gen = torch.Generator(device=dev)
-        gen.manual_seed(9 + rank)
+        comm = TPComm(max_N=max(c[1] for c in CASES))
+        for ci, (name, N, K, Ms, split) in enumerate(CASES):
+            P = make_np_parts(np.random.default_rng(100 + ci), N, K, 128, 0.005, 16)
+            Kp = K // world
+            S = P.shard(rank * Kp, (rank + 1) * Kp)
+            T = dev_layer(S)
+            lut = _C.prepack_lut(T["lut"], torch.bfloat16)
+            cols, vals = _C.prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], N, Kp, 4,
+                                             torch.bfloat16, S.G, S.goff)
+            A = T["A"].to(torch.bfloat16).contiguous()
 
-        def fused(x, h, out, in_kernel_h=False):
-            if in_kernel_h:  # this rank's columns of A, h = A x computed in the kernel
-                _C.gemv_allreduce(comm, x, L.q_packed, lut, out, N, Kp, 4, L.words_per_row, L.chunk_offsets, cols,
-                                  vals, None, L.lora_B, L.dora_gamma, L.lora_scale, L.group_size, L.group_offset,
-                                  fmt, lora_A=L.lora_A_act)
-                return
-            _C.gemv_allreduce(comm, x, L.q_packed, lut, out, N, Kp, 4, L.words_per_row, L.chunk_offsets, cols,
-                              vals, h, L.lora_B, L.dora_gamma, L.lora_scale, L.group_size, L.group_offset, fmt)
+            def fused(x, y, h=None):
+                _C.gemv_allreduce(comm, x, T["q"], lut, y, N, Kp, 4, S.wpr, T["off"], cols, vals, h, T["B"],
+                                  T["gamma"], S.scale, S.G, S.goff, 1, lora_A=None if h is not None else A)
 
-        def check(x, h, y):
-            own = S.forward(L, x, h=h).float()
-            parts = [torch.empty_like(own) for _ in range(2)]
-            dist.all_gather(parts, own)
-            ref = parts[0] + parts[1]
-            errs.append(float((y.float() - ref).abs().max() / ref.abs().max()))
-
-        for M in (1, 5, 16):
-            for i in range(4):  # repeated calls: epochs and slot parity advance
-                x = torch.randn((M, Kp), generator=gen, device=dev).to(torch.bfloat16)
-                h = S.lora_h(L, x)
-                y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-                fused(x, h, y, in_kernel_h=i % 2 == 1)
-                check(x, h, y)
-        # a down-proj shard (K = 9472 per rank): the K split takes a cluster of
-        # more than 8 CTAs, whose reduction feeds the exchange
-        Kd = 9472
-        Ld = S.make_layer(N, Kd, group_size=128, density=0.005, r=16, seed=60 + rank, device=dev)
-        Ld.prepack(torch.bfloat16)
-        lutd, colsd, valsd, fmtd = Ld.operands_for(torch.bfloat16)
-        for M in (1, 16):
-            x = torch.randn((M, Kd), generator=gen, device=dev).to(torch.bfloat16)
-            h = S.lora_h(Ld, x)
-            y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-            _C.gemv_allreduce(comm, x, Ld.q_packed, lutd, y, N, Kd, 4, Ld.words_per_row, Ld.chunk_offsets, colsd,
-                              valsd, None, Ld.lora_B, Ld.dora_gamma, Ld.lora_scale, Ld.group_size, Ld.group_offset,
-                              fmtd, lora_A=Ld.lora_A_act)
-            own = S.forward(Ld, x, h=h).float()
-            parts = [torch.empty_like(own) for _ in range(2)]
-            dist.all_gather(parts, own)
-            ref = parts[0] + parts[1]
-            errs.append(float((y.float() - ref).abs().max() / ref.abs().max()))
-        # the same inside a CUDA graph, replayed with new inputs
+            if split:
+                _lib.check(_lib.lib.wlq_gemv_set_split(split), "wlq_gemv_set_split")
+            try:
+                for M in Ms:
+                    for i in range(3):  # repeated calls: epochs and slot parity advance
+                        x = _inputs(1000 * ci + 10 * M + i, K, M)[:, rank * Kp:(rank + 1) * Kp].contiguous().to(dev)
+                        y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=dev)
+                        if i % 2 == 0:  # h = A x of this rank's columns inside the kernel
+                            fused(x, y)
+                        else:           # h given
+                            fused(x, y, _C.lora_h(x, A))
+                        torch.cuda.synchronize()
+                        out[(name, M, i)] = y.float().cpu().numpy()
+                if split:
+                    out[(name, "split")] = int(_lib.lib.wlq_gemv_last_split())
+            finally:
+                _lib.check(_lib.lib.wlq_gemv_set_split(0), "wlq_gemv_set_split")
+        # a CUDA graph of the o shard, replayed with new inputs
+        name, N, K, _, _ = CASES[0]
+        P = make_np_parts(np.random.default_rng(100), N, K, 128, 0.005, 16)
+        Kp = K // world
+        S = P.shard(rank * Kp, (rank + 1) * Kp)
+        T = dev_layer(S)
+        lut = _C.prepack_lut(T["lut"], torch.bfloat16)
+        cols, vals = _C.prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], N, Kp, 4,
+                                         torch.bfloat16, S.G, S.goff)
+        A = T["A"].to(torch.bfloat16).contiguous()
         M = 8
-        x = torch.randn((M, Kp), generator=gen, device=dev).to(torch.bfloat16)
-        h = S.lora_h(L, x)
+        x = torch.empty((M, Kp), dtype=torch.bfloat16, device=dev)
         y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-        fused(x, h, y)
+
+        def call():
+            _C.gemv_allreduce(comm, x, T["q"], lut, y, N, Kp, 4, S.wpr, T["off"], cols, vals, None, T["B"],
+                              T["gamma"], S.scale, S.G, S.goff, 1, lora_A=A)
+
+        x.copy_(_inputs(77, K, M)[:, rank * Kp:(rank + 1) * Kp].to(dev))
+        call()
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                fused(x, h, y)
+                call()
         torch.cuda.current_stream().wait_stream(s)
-        for _ in range(3):
-            x.copy_(torch.randn((M, Kp), generator=gen, device=dev).to(torch.bfloat16))
-            h.copy_(S.lora_h(L, x))
+        for i in range(3):
+            x.copy_(_inputs(500 + i, K, M)[:, rank * Kp:(rank + 1) * Kp].to(dev))
             dist.barrier()
             g.replay()
             torch.cuda.synchronize()
-            check(x, h, y)
+            out[("graph", M, i)] = y.float().cpu().numpy()
         del g
         torch.cuda.synchronize()
-        results[rank] = {"errs": errs, "flag": comm.error()}
+        out["flag"] = comm.error()
+        results[rank] = out
     finally:
         dist.barrier()
         if comm is not None:
@@ -117,26 +135,51 @@ def _rank_main(rank, port, results):
         dist.destroy_process_group()
 
 
-def test_fused_allreduce_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_allreduce_matches_unsharded_oracle(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, port, results)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, results)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=600)
+        p.join(timeout=900)
     for p in procs:
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    for r in range(2):
-        res = dict(results[r])
-        assert res["flag"] == 0, res
-        assert max(res["errs"]) <= 1e-2, res
+    res = [dict(results[r]) for r in range(world)]
+    assert all(r["flag"] == 0 for r in res), [r["flag"] for r in res]
+    # every rank holds the same sum, bit for bit
+    keys = [k for k in res[0] if k != "flag" and not (isinstance(k, tuple) and k[1] == "split")]
+    for k in keys:
+        for r in range(1, world):
+            assert np.array_equal(res[0][k], res[r][k]), (k, r)
+    # against the oracle's float64 forward of the unsharded layer
+    for ci, (name, N, K, Ms, split) in enumerate(CASES):
+        P = make_np_parts(np.random.default_rng(100 + ci), N, K, 128, 0.005, 16)
+        L = P.full()
+        W = L.dense()
+        if split:
+            assert all(r[(name, "split")] == split for r in res), [r[(name, "split")] for r in res]
+        for M in Ms:
+            for i in range(3):
+                x = _inputs(1000 * ci + 10 * M + i, K, M).float().numpy()
+                h = x.astype(np.float64) @ P.A.astype(np.float64).T
+                ref = O.forward_f64(W, x, h, P.B, P.gamma, P.scale)
+                e = rel_err(res[0][(name, M, i)], ref)
+                assert e <= TOL, (name, M, i, e)
+    P = make_np_parts(np.random.default_rng(100), *CASES[0][1:3], 128, 0.005, 16)
+    W = P.full().dense()
+    for i in range(3):
+        x = _inputs(500 + i, CASES[0][2], 8).float().numpy()
+        h = x.astype(np.float64) @ P.A.astype(np.float64).T
+        e = rel_err(res[0][("graph", 8, i)], O.forward_f64(W, x, h, P.B, P.gamma, P.scale))
+        assert e <= TOL, ("graph", i, e)
 
 
 def test_fused_allreduce_wait_runs_out():
