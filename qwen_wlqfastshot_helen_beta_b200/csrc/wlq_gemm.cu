@@ -506,37 +506,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------- host side
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-    });
-    return fn;
-}
-
-int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz, const char* what) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return fail(WLQ_ERR_CUDA, "wlq_gemm: cuTensorMapEncodeTiled is not available from the driver");
-    const cuuint64_t dims[2] = {inner, outer};
-    const cuuint64_t strides[1] = {row_bytes};
-    const cuuint32_t box[2] = {box_inner, box_outer};
-    const cuuint32_t es[2] = {1, 1};
-    const CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(WLQ_ERR_CUDA, "wlq_gemm: tensor map for %s rejected (CUresult %d)", what, (int)r);
-    return WLQ_OK;
-}
-
 template <typename T, int NACC, int NPG, bool PREPACKED, int BN>
 int launch_tiles(const GemmParams& p, cudaStream_t stream) {
     using P = Plan<NACC, NPG, BN>;
@@ -658,14 +627,11 @@ int read_device_error(int device, unsigned int* flags, int clear) {
     cudaError_t e = cudaGetDevice(&prev);
     if (e != cudaSuccess) return check_cuda(e, "cudaGetDevice");
     if (device != prev && (e = cudaSetDevice(device)) != cudaSuccess) return check_cuda(e, "cudaSetDevice");
+    // only this translation unit's kernels wait on mbarriers
     unsigned int v = 0;
-    e = cudaMemcpyFromSymbol(&v, g_wlq_device_error, sizeof(v));
-    if (e == cudaSuccess && clear) {
-        const unsigned int z = 0;
-        e = cudaMemcpyToSymbol(g_wlq_device_error, &z, sizeof(z));
-    }
+    const int rc = tu_device_error(&v, clear);
     if (device != prev) cudaSetDevice(prev);
-    if (e != cudaSuccess) return check_cuda(e, "device error word");
+    if (rc) return rc;
     *flags = v;
     return WLQ_OK;
 }

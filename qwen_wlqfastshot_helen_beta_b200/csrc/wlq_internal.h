@@ -1,6 +1,7 @@
 // Host-side plumbing shared by the translation units of libwlq_b200.so.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -75,6 +76,12 @@ int launch_dequant(const uint32_t* q, const uint16_t* lut, uint16_t* W, const in
 
 // Reads (and optionally clears) the device error word of `device`.
 int read_device_error(int device, unsigned int* flags, int clear);
+
+// 2-D tensor map (TMA descriptor) of a row-major [outer, inner] array with
+// rows of row_bytes, box box_inner x box_outer elements; rejected shapes give
+// WLQ_ERR_CUDA.  Loads past the array's edges read zeros.
+int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz, const char* what);
 
 // Multiprocessor count of the current device (cached per device).
 int device_sm_count();

@@ -27,7 +27,7 @@ constexpr int kHStages = 3;
 constexpr int kHTile = 64 * 128;                      // bytes of one 64 x 64 tile of 16-bit values
 constexpr int kHSmem = kHStages * 2 * kHTile;         // X and A tiles per stage
 constexpr int kHPartStride = kHRank + 4;              // fp32 partial tile row stride (floats)
-constexpr int kHMaxSplit = 8;
+constexpr int kHMaxSplit = 16;  // above 8: a non-portable cluster size
 static_assert(kHTok * kHPartStride * 4 <= kHSmem, "the partial tile reuses the ring");
 
 struct HParams {
@@ -163,6 +163,10 @@ __global__ void __launch_bounds__(128) lora_h_rows_kernel(const HParams p) {
     }
 }
 
+// Returns kHRefused (the error cleared) when the device refuses a cluster of
+// more than 8 CTAs; the caller retries at 8.
+constexpr int kHRefused = -1;
+
 template <typename T>
 int launch_h(const HParams& p, int gx, int ks, int gz, bool vec, cudaStream_t stream) {
     if (!vec) {
@@ -172,6 +176,13 @@ int launch_h(const HParams& p, int gx, int ks, int gz, bool vec, cudaStream_t st
     auto kern = lora_h_kernel<T>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kHSmem);
     if (e != cudaSuccess) return check_cuda(e, "lora_h_kernel smem attribute");
+    if (ks > 8) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return kHRefused;
+        }
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)gx, (unsigned)ks, (unsigned)gz);
     cfg.blockDim = dim3(128, 1, 1);
@@ -184,7 +195,14 @@ int launch_h(const HParams& p, int gx, int ks, int gz, bool vec, cudaStream_t st
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = ks > 1 ? 1 : 0;
-    return check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "lora_h_kernel launch");
+    e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess && ks > 8 &&
+        (e == cudaErrorInvalidClusterSize || e == cudaErrorLaunchOutOfResources || e == cudaErrorInvalidValue ||
+         e == cudaErrorNotSupported)) {
+        cudaGetLastError();
+        return kHRefused;
+    }
+    return check_cuda(e, "lora_h_kernel launch");
 }
 
 }  // namespace
@@ -204,15 +222,22 @@ int launch_lora_h(const void* X, const void* A, float* H, int M, int K, int r, i
                      (reinterpret_cast<uintptr_t>(A) & 15) == 0;
     const int gx = (M + kHTok - 1) / kHTok;
     const int gz = (r + kHRank - 1) / kHRank;
-    // split K over a cluster until about two CTAs per SM are in flight,
-    // keeping at least two k tiles per rank; no rank left empty
+    // split K over a cluster (up to 16 CTAs) until about two CTAs per SM are
+    // in flight, keeping at least two k tiles per rank; no rank left empty
     const int sms = device_sm_count();
-    int ks = 1;
-    while (ks < kHMaxSplit && (int64_t)gx * gz * ks < 2LL * sms && p.ktiles >= 2 * (ks + 1)) ++ks;
-    p.ktiles_per_rank = (p.ktiles + ks - 1) / ks;
-    ks = (p.ktiles + p.ktiles_per_rank - 1) / p.ktiles_per_rank;
-    return dtype == WLQ_DTYPE_BF16 ? launch_h<__nv_bfloat16>(p, gx, ks, gz, vec, stream)
-                                   : launch_h<__half>(p, gx, ks, gz, vec, stream);
+    auto plan = [&](int cap) {
+        int ks = 1;
+        while (ks < cap && (int64_t)gx * gz * ks < 2LL * sms && p.ktiles >= 2 * (ks + 1)) ++ks;
+        p.ktiles_per_rank = (p.ktiles + ks - 1) / ks;
+        return (p.ktiles + p.ktiles_per_rank - 1) / p.ktiles_per_rank;
+    };
+    auto run = [&](int ks) {
+        return dtype == WLQ_DTYPE_BF16 ? launch_h<__nv_bfloat16>(p, gx, ks, gz, vec, stream)
+                                       : launch_h<__half>(p, gx, ks, gz, vec, stream);
+    };
+    int rc = run(plan(kHMaxSplit));
+    if (rc == kHRefused) rc = run(plan(8));
+    return rc;
 }
 
 }  // namespace wlq

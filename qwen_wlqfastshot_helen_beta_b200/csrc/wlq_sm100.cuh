@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "wlq_common.cuh"
+#include "wlq_internal.h"
 
 namespace wlq {
 
@@ -17,6 +18,20 @@ namespace wlq {
 static __device__ unsigned int g_wlq_device_error = 0;
 constexpr unsigned int kErrWaitTimeout = 1u;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Reads (and with `clear` zeroes) this translation unit's word on the
+// current device.  Synchronous.
+static inline int tu_device_error(unsigned int* flags, int clear) {
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_wlq_device_error, sizeof(v));
+    if (e == cudaSuccess && clear) {
+        const unsigned int z = 0;
+        e = cudaMemcpyToSymbol(g_wlq_device_error, &z, sizeof(z));
+    }
+    if (e != cudaSuccess) return check_cuda(e, "device error word");
+    *flags = v;
+    return WLQ_OK;
+}
 
 
 // ---------------------------------------------------------------- mbarrier
