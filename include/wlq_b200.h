@@ -115,6 +115,27 @@ WLQ_API int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, 
              int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
              int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
 
+/* wlq_gemm with a stream-K schedule for the tensor-core path (M > 16 rows
+ * that the GEMV does not take): when the output tiles do not fill whole
+ * waves of one CTA per SM, the k steps of the last wave and the remainder are
+ * split evenly over the SMs and the partial tiles are summed through
+ * `workspace` (fp32, in a fixed CTA order, so results do not depend on
+ * timing).  `workspace` is device memory of workspace_bytes, 256-byte aligned,
+ * zero-filled before its first use and kept between calls (every call leaves
+ * its flags zero again); wlq_gemm_workspace_bytes(device) bytes always
+ * suffice, less restricts the split.  Calls that share a workspace must not
+ * run concurrently (one stream, or one workspace per stream).  NULL or too
+ * small a workspace gives wlq_gemm's data-parallel schedule.  Replaces the same
+ * reference composition as wlq_gemm (csrc/vllm_binding.cpp:355-393), where
+ * cuBLAS picks split-K schedules internally. */
+WLQ_API size_t wlq_gemm_workspace_bytes(int device);
+WLQ_API int wlq_gemm_streamk(const void* X, const int32_t* q_packed, const void* lut_c, void* out,
+             const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
+             const float* lora_H, const void* lora_B, const void* dora_gamma, float lora_scale,
+             int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
+             int lut_group_offset, int lut_format, int act_dtype, void* workspace, size_t workspace_bytes,
+             wlq_stream_t stream);
+
 /* DoRA low-rank input H = X lora_A^T, fp32 [M, r], for the calls that do not
  * compute it inside the decode GEMV (the prefill GEMM; rank above 48).  X
  * [M, K] and lora_A [r, K] in act_dtype; tensor cores, fp32 accumulation, no

@@ -219,21 +219,53 @@ def gemv_lora_a(q_packed, lut_c, x, out, N, K, bits, chunk_offsets, chunk_cols, 
     check(rc, "wlq_gemv_lora_a")
 
 
+# One stream-K workspace per device (wlq_gemm_streamk), allocated and zeroed
+# on the device's first GEMM call outside CUDA-graph capture and kept for the
+# process (its flags are left zero by every call).  The torch ops run on one
+# stream per device, as vLLM runs a model; calls on several streams at once
+# would share it and must use gemm_forward(..., workspace=False).
+_GEMM_WS = {}
+
+
+def gemm_workspace(dev: torch.device):
+    """This device's stream-K workspace, or None while a CUDA graph is being
+    captured before it exists (the call then takes the data-parallel
+    schedule)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _GEMM_WS.get(idx)
+    if ws is None:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        nbytes = int(lib.wlq_gemm_workspace_bytes(idx))
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _GEMM_WS[idx] = ws
+    return ws
+
+
 def gemm_forward(X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,
                  chunk_vals=None, lora_H=None, lora_B=None, dora_gamma=None, lora_scale=1.0, lut_group_size=0,
-                 lut_group_offset=0, lut_format=WLQ_LUT_F16):
-    """Batched forward for any M (csrc/vllm_binding.cpp:318-419)."""
+                 lut_group_offset=0, lut_format=WLQ_LUT_F16, workspace=True):
+    """Batched forward for any M (csrc/vllm_binding.cpp:318-419).  The
+    tensor-core path takes the stream-K schedule with this device's
+    workspace (workspace=False: the data-parallel schedule of wlq_gemm)."""
     N, K, bits, wpr = int(N), int(K), int(bits), int(words_per_row)
     offs, cols, vals = _opt(chunk_offsets), _opt(chunk_cols), _opt(chunk_vals)
     lb, lh, gm = _opt(lora_B), _opt(lora_H), _opt(dora_gamma)
     M, r = _linear_checks("gemm_forward", X, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lb, lh, gm,
                           int(lut_group_size), int(lut_group_offset), int(lut_format))
+    ws = gemm_workspace(X.device) if workspace and M > 16 else None
     with _DeviceGuard(X.device):
-        rc = lib.wlq_gemm(_ptr(X), _ptr(q_packed), _ptr(lut_c), _ptr(out), _ptr(offs), _ptr(cols), _ptr(vals),
-                          _ptr(lh), _ptr(lb), _ptr(gm), float(lora_scale), r, M, N, K, bits, wpr,
-                          int(lut_group_size), int(lut_group_offset), int(lut_format), _act_dtype(X),
-                          _stream(X.device))
-    check(rc, "wlq_gemm")
+        if ws is not None:
+            rc = lib.wlq_gemm_streamk(_ptr(X), _ptr(q_packed), _ptr(lut_c), _ptr(out), _ptr(offs), _ptr(cols),
+                                      _ptr(vals), _ptr(lh), _ptr(lb), _ptr(gm), float(lora_scale), r, M, N, K, bits,
+                                      wpr, int(lut_group_size), int(lut_group_offset), int(lut_format),
+                                      _act_dtype(X), _ptr(ws), ws.numel(), _stream(X.device))
+        else:
+            rc = lib.wlq_gemm(_ptr(X), _ptr(q_packed), _ptr(lut_c), _ptr(out), _ptr(offs), _ptr(cols), _ptr(vals),
+                              _ptr(lh), _ptr(lb), _ptr(gm), float(lora_scale), r, M, N, K, bits, wpr,
+                              int(lut_group_size), int(lut_group_offset), int(lut_format), _act_dtype(X),
+                              _stream(X.device))
+    check(rc, "wlq_gemm_streamk" if ws is not None else "wlq_gemm")
 
 
 def gemv_allreduce(comm, X, q_packed, lut_c, out, N, K, bits, words_per_row, chunk_offsets=None, chunk_cols=None,

@@ -190,6 +190,37 @@ int wlq_gemm(const void* X, const int32_t* q_packed, const void* lut_c, void* ou
     return launch_gemm(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+size_t wlq_gemm_workspace_bytes(int device) {
+    g_last_error[0] = '\0';
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess) return 0;
+    if (device != prev && cudaSetDevice(device) != cudaSuccess) return 0;
+    const size_t b = gemm_workspace_bytes();
+    if (device != prev) cudaSetDevice(prev);
+    return b;
+}
+
+int wlq_gemm_streamk(const void* X, const int32_t* q_packed, const void* lut_c, void* out,
+                     const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
+                     const float* lora_H, const void* lora_B, const void* dora_gamma, float lora_scale, int r, int M,
+                     int N, int K, int bits, int words_per_row, int lut_group_size, int lut_group_offset,
+                     int lut_format, int act_dtype, void* workspace, size_t workspace_bytes, wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    LinearArgs a;
+    int rc = build_args("wlq_gemm_streamk", X, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals, lora_B,
+                        lora_H, nullptr, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row, lut_group_size,
+                        lut_group_offset, lut_format, act_dtype, a);
+    if (rc) return rc;
+    if (workspace && !aligned(workspace, 256))
+        return fail(WLQ_ERR_ALIGNMENT, "wlq_gemm_streamk: the workspace must be 256-byte aligned");
+    if (M == 0 || N == 0) return WLQ_OK;
+    if ((rc = require_sm100())) return rc;
+    if (gemv_preferred(M, N, K, a.lut_prepacked, X)) return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
+    a.ws = workspace;
+    a.ws_bytes = workspace ? workspace_bytes : 0;
+    return launch_gemm(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int wlq_lora_h(const void* X, const void* lora_A, float* H, int M, int K, int r, int act_dtype,
                wlq_stream_t stream) {
     g_last_error[0] = '\0';

@@ -38,6 +38,10 @@ struct LinearArgs {
     int ncsr;                // outlier chunks per row
     int dtype;               // WLQ_DTYPE_*
     bool lut_prepacked;      // WLQ_LUT_PREPACKED codebooks
+    // stream-K workspace of the tensor-core GEMM (wlq_gemm_streamk): flags
+    // then partial tiles; null = data-parallel schedule only
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
     // fused tensor-parallel all-reduce (wlq_gemv_allreduce); tp_world = 1: off
     int tp_world = 1, tp_rank = 0, tp_nmax = 0;
     void* tp_bufs[8] = {};   // every rank's communication buffer (this process's mappings)
@@ -64,6 +68,9 @@ constexpr TpLayout tp_layout(int world, int max_N) {
 
 int launch_gemv(const LinearArgs& a, cudaStream_t stream);
 int launch_gemm(const LinearArgs& a, cudaStream_t stream);
+// Workspace bytes of the stream-K schedule on the current device: flags plus
+// one partial tile of the largest CTA shape per SM.
+size_t gemm_workspace_bytes();
 int launch_lora_h(const void* X, const void* A, float* H, int M, int K, int r, int dtype, cudaStream_t stream);
 int launch_prepack_outliers(const uint32_t* q, const uint16_t* lut, const int32_t* off, const uint16_t* ccols,
                             const uint8_t* cvals, int N, int K, int wpr, int group_size, int goff, int ngroups,

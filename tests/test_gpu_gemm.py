@@ -156,3 +156,51 @@ def test_gemm_cta_shapes(N, K, M):
         y = S.forward(L.prepack(dt) if dt != torch.bfloat16 else L, xx, h=h)
         e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
         assert e <= 2e-2, (N, K, M, dt, e)
+
+
+# ------------------------------------------------------------ stream-K
+
+SK_CASES = [
+    # N, K, M, G, r: o/down-like shapes whose tiles do not fill whole waves
+    (3584, 3584, 512, 128, 16),    # 28 tiles of 256 x 256: every tile split over several CTAs
+    (3584, 18944, 512, 128, 16),   # long K: many steps per CTA, low-rank step in a later segment
+    (3584, 3584, 8192, 128, 16),   # 448 tiles: 2 data-parallel waves, then stream-K over the rest
+    (1000, 1100, 300, 0, 80),      # ragged N, M and K, per-row codebooks, two low-rank steps
+    (4736, 2368, 2048, 128, 16),   # a tensor-parallel shard shape
+    (256, 512, 64, 128, 16),       # one tile split over a few CTAs
+]
+
+
+@pytest.mark.parametrize("case", SK_CASES, ids=lambda c: f"N{c[0]}K{c[1]}M{c[2]}G{c[3]}r{c[4]}")
+def test_gemm_streamk_matches_oracle(case):
+    """wlq_gemm_streamk (the stream-K schedule: partial tiles summed through
+    the workspace in CTA order) against the oracle and against the
+    data-parallel schedule, on both codebook layouts; repeated calls give the
+    same bits (the fix-up order is fixed) and leave the workspace flags zero."""
+    from qwen_wlqfastshot_helen_beta_b200 import _C as CC
+    N, K, M, G, r = case
+    rng = np.random.default_rng(N + K + M)
+    L = make_np_layer(rng, N, K, G, 0, density=0.005, r=r)
+    T = dev_layer(L)
+    dtype = torch.bfloat16
+    x, h = inputs(rng, L, M, dtype)
+    ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+    lutp = CC.prepack_lut(T["lut"], dtype)
+    colsp, valsp = CC.prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], N, K, 4, dtype, G, 0)
+    for lut, cols, vals, fmt in ((lutp, colsp, valsp, 1), (T["lut"], T["cols"], T["vals"], 0)):
+        ys = []
+        for ws in (True, True, False):
+            y = torch.full((M, N), float("nan"), dtype=dtype, device="cuda")
+            CC.gemm_forward(x, T["q"], lut, y, N, K, 4, L.wpr, T["off"], cols, vals, h, T["B"], T["gamma"], L.scale,
+                            G, 0, fmt, workspace=ws)
+            torch.cuda.synchronize()
+            assert CC.device_error() == 0
+            assert torch.isfinite(y).all(), (fmt, ws)
+            e = rel_err(y.float().cpu().numpy(), ref)
+            assert e <= 2e-2, (fmt, ws, e)
+            ys.append(y)
+        assert torch.equal(ys[0], ys[1]), fmt  # deterministic
+        assert rel_err(ys[0].float().cpu().numpy(), ys[2].float().cpu().numpy()) <= 1e-2, fmt
+    ws = CC.gemm_workspace(torch.device("cuda"))
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert int(ws[:4 * sms].view(torch.int32).abs().sum()) == 0  # flags left zero
