@@ -59,8 +59,12 @@ __global__ void __launch_bounds__(128) lora_h_kernel(const HParams p) {
     auto xs = [&](int s) { return sb + (uint32_t)(s * 2 * kHTile); };
     auto as = [&](int s) { return sb + (uint32_t)(s * 2 * kHTile + kHTile); };
 
-    // k tile kt into stage s: 512 16-byte pieces of X and of A, 4 + 4 per
-    // thread; rows past M or r and columns past K (K % 8 == 0) read as zero
+    // ranks of this CTA in MMA n-tile pairs (16 ranks each): only these rows
+    // of A are loaded and multiplied
+    const int npairs = min(4, (p.r - j0 + 15) / 16);
+    // k tile kt into stage s: 512 16-byte pieces of X (4 per thread) and the
+    // 16 npairs rows of A; rows past M or r and columns past K (K % 8 == 0)
+    // read as zero
     auto issue = [&](int kt, int s) {
         if (kt < kt1) {
 #pragma unroll
@@ -70,9 +74,11 @@ __global__ void __launch_bounds__(128) lora_h_kernel(const HParams p) {
                 const int k = kt * kHK + ch * 8;
                 const bool kok = k < p.K;
                 const bool xok = kok && m0 + row < p.M;
-                const bool aok = kok && j0 + row < p.r;
                 cp_async16(xs(s) + hswz(row, ch), p.X + (xok ? (int64_t)(m0 + row) * p.K + k : 0), xok);
-                cp_async16(as(s) + hswz(row, ch), p.A + (aok ? (int64_t)(j0 + row) * p.K + k : 0), aok);
+                if (row < 16 * npairs) {
+                    const bool aok = kok && j0 + row < p.r;
+                    cp_async16(as(s) + hswz(row, ch), p.A + (aok ? (int64_t)(j0 + row) * p.K + k : 0), aok);
+                }
             }
         }
         cp_async_commit();
@@ -100,6 +106,7 @@ __global__ void __launch_bounds__(128) lora_h_kernel(const HParams p) {
             }
 #pragma unroll
             for (int np = 0; np < 4; ++np) {  // ranks 16 np .. +15: two MMA n-tiles
+                if (np >= npairs) break;
                 const int row = np * 16 + (lane & 7) + 8 * (lane >> 4);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(as(st) + hswz(row, 2 * kk + ((lane >> 3) & 1)), b0, b1, b2, b3);
