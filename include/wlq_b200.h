@@ -136,6 +136,31 @@ WLQ_API int wlq_gemm_streamk(const void* X, const int32_t* q_packed, const void*
              int lut_group_offset, int lut_format, int act_dtype, void* workspace, size_t workspace_bytes,
              wlq_stream_t stream);
 
+/* wlq_gemm_streamk for callers that cannot allocate device memory: a host
+ * runtime reaching this library through FFI (cgo, JNI, ctypes) with no device
+ * allocator of its own, or a serving loop that must not call cudaMalloc on
+ * its hot path because cudaMalloc synchronises the device and cannot be
+ * recorded while a stream is being captured.  It allocates nothing: its
+ * stream-K scratch (flags and partial tiles) is a static array of
+ * WLQ_GEMM_STATIC_SCRATCH_BYTES inside the library, which every GPU that
+ * loads the library holds until the process exits.  Same arguments and
+ * results as wlq_gemm_streamk without the workspace.  The first call on a
+ * device looks the array's device address up (cudaGetSymbolAddress, with
+ * that device current): make it before any stream capture.  Each call
+ * clears the scratch's flags on `stream` first; the array keeps the last
+ * call's partial tiles.  Calls on one device share the array: calls that
+ * overlap on the GPU (several streams, or several threads) race and give
+ * wrong results.  A problem whose schedule needs more scratch than the
+ * array holds is refused with WLQ_ERR_CAPACITY (on a 148-SM B200 every
+ * schedule fits: 148 partial tiles of 256 KB plus flags).  No counterpart in
+ * the reference, whose GEMM path allocates through ATen. */
+#define WLQ_GEMM_STATIC_SCRATCH_BYTES (40u * 1024u * 1024u)
+WLQ_API int wlq_gemm_streamk_noalloc(const void* X, const int32_t* q_packed, const void* lut_c, void* out,
+             const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
+             const float* lora_H, const void* lora_B, const void* dora_gamma, float lora_scale,
+             int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
+             int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream);
+
 /* DoRA low-rank input H = X lora_A^T, fp32 [M, r], for the calls that do not
  * compute it inside the decode GEMV (the prefill GEMM; rank above 48).  X
  * [M, K] and lora_A [r, K] in act_dtype; tensor cores, fp32 accumulation, no

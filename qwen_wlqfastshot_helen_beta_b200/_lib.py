@@ -33,6 +33,8 @@ SIGNATURES = {
                         _i32, _i32, _i32, _i32, _p]),
     "wlq_lora_h": (_i32, [_p, _p, _p, _i32, _i32, _i32, _i32, _p]),
     "wlq_gemm_workspace_bytes": (ctypes.c_size_t, [_i32]),
+    "wlq_gemm_streamk_noalloc": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32,
+                                        _i32, _i32, _i32, _i32, _i32, _p]),
     "wlq_gemm_streamk": (_i32, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f32, _i32, _i32, _i32, _i32, _i32, _i32,
                                 _i32, _i32, _i32, _i32, _p, ctypes.c_size_t, _p]),
     "wlq_prepack_lut": (_i32, [_p, _p, _i64, _i32, _p]),

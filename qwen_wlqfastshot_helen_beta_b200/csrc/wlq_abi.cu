@@ -221,6 +221,24 @@ int wlq_gemm_streamk(const void* X, const int32_t* q_packed, const void* lut_c, 
     return launch_gemm(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int wlq_gemm_streamk_noalloc(const void* X, const int32_t* q_packed, const void* lut_c, void* out,
+                             const int32_t* chunk_offsets, const void* chunk_cols, const void* chunk_vals,
+                             const float* lora_H, const void* lora_B, const void* dora_gamma, float lora_scale,
+                             int r, int M, int N, int K, int bits, int words_per_row, int lut_group_size,
+                             int lut_group_offset, int lut_format, int act_dtype, wlq_stream_t stream) {
+    g_last_error[0] = '\0';
+    LinearArgs a;
+    int rc = build_args("wlq_gemm_streamk_noalloc", X, q_packed, lut_c, out, chunk_offsets, chunk_cols, chunk_vals,
+                        lora_B, lora_H, nullptr, dora_gamma, lora_scale, r, M, N, K, bits, words_per_row,
+                        lut_group_size, lut_group_offset, lut_format, act_dtype, a);
+    if (rc) return rc;
+    if (M == 0 || N == 0) return WLQ_OK;
+    if ((rc = require_sm100())) return rc;
+    // up to 16 tokens the GEMV runs: it needs no scratch
+    if (gemv_preferred(M, N, K, a.lut_prepacked, X)) return launch_gemv(a, reinterpret_cast<cudaStream_t>(stream));
+    return launch_gemm_noalloc(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int wlq_lora_h(const void* X, const void* lora_A, float* H, int M, int K, int r, int act_dtype,
                wlq_stream_t stream) {
     g_last_error[0] = '\0';

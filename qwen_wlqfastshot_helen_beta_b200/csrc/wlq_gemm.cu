@@ -879,6 +879,66 @@ size_t gemm_workspace_bytes() {
     return ((size_t)sms * 4 + 255) / 256 * 256 + (size_t)sms * (2 * kTileM) * 256 * 4;
 }
 
+// ------------------------------------------- stream-K without allocation
+// Scratch of wlq_gemm_streamk_noalloc: a file-scope device array, so callers
+// that cannot allocate device memory still get the stream-K schedule.  Every
+// GPU that loads the library holds it (zero-filled at load) until the process
+// exits; all calls on a device share it.
+static __device__ __align__(256) unsigned char g_static_scratch[WLQ_GEMM_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_static_mu;
+void* g_static_ptr[64] = {};  // device address of g_static_scratch, per device
+}  // namespace
+
+int launch_gemm_noalloc(const LinearArgs& a0, cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return check_cuda(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(WLQ_ERR_DEVICE, "wlq_gemm_streamk_noalloc: device %d out of range", dev);
+    void* scratch = nullptr;
+    {
+        // set-up once per device, with that device current: in host code the
+        // array's name is only a stand-in, so the kernels get its device
+        // address from the runtime
+        std::lock_guard<std::mutex> lock(g_static_mu);
+        if (!g_static_ptr[dev]) {
+            void* ptr = nullptr;
+            e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+            if (e != cudaSuccess) return check_cuda(e, "wlq_gemm_streamk_noalloc: cudaGetSymbolAddress");
+            g_static_ptr[dev] = ptr;
+        }
+        scratch = g_static_ptr[dev];
+    }
+    // the scratch this call's schedule needs: the schedule a full workspace
+    // would give (flags plus one partial tile per stream-K CTA)
+    const int sms = device_sm_count();
+    const size_t flag_bytes = ((size_t)sms * 4 + 255) / 256 * 256;
+    const int steps = (a0.K + kBK - 1) / kBK + (a0.r > 0 ? (a0.r + kBK - 1) / kBK : 0);
+    const size_t full_part = gemm_workspace_bytes() - flag_bytes;
+    const struct { int nacc, bn; double eff; } shapes[3] = {{2, 256, 1.0}, {2, 128, 0.85}, {1, 128, 0.55}};
+    Sched sc{};
+    sc.cost = 1e300;
+    for (const auto& sh : shapes) {
+        const Sched c = plan_shape(sh.nacc, sh.bn, sh.eff, a0.M, a0.N, steps, sms, full_part);
+        if (c.cost < sc.cost * (1.0 - 1e-9)) sc = c;
+    }
+    const size_t need = sc.sk_ctas > 0 ? flag_bytes + (size_t)sc.sk_ctas * sc.nacc * kTileM * sc.bn * 4 : 0;
+    if (need > WLQ_GEMM_STATIC_SCRATCH_BYTES)
+        return fail(WLQ_ERR_CAPACITY,
+                    "wlq_gemm_streamk_noalloc: M=%d N=%d K=%d needs %zu bytes of stream-K scratch, more than the "
+                    "library's static %zu; use wlq_gemm_streamk with a workspace", a0.M, a0.N, a0.K, need,
+                    (size_t)WLQ_GEMM_STATIC_SCRATCH_BYTES);
+    // the flags must start at zero: a call that gave up waiting may have
+    // left some set
+    e = cudaMemsetAsync(scratch, 0, flag_bytes, stream);
+    if (e != cudaSuccess) return check_cuda(e, "wlq_gemm_streamk_noalloc: clearing the flags");
+    LinearArgs a = a0;
+    a.ws = scratch;
+    a.ws_bytes = WLQ_GEMM_STATIC_SCRATCH_BYTES;
+    return launch_gemm(a, stream);
+}
+
 int read_device_error(int device, unsigned int* flags, int clear) {
     int prev = 0;
     cudaError_t e = cudaGetDevice(&prev);

@@ -71,6 +71,8 @@ int launch_gemm(const LinearArgs& a, cudaStream_t stream);
 // Workspace bytes of the stream-K schedule on the current device: flags plus
 // one partial tile of the largest CTA shape per SM.
 size_t gemm_workspace_bytes();
+// The stream-K GEMM on the library's static scratch (wlq_gemm_streamk_noalloc).
+int launch_gemm_noalloc(const LinearArgs& a, cudaStream_t stream);
 int launch_lora_h(const void* X, const void* A, float* H, int M, int K, int r, int dtype, cudaStream_t stream);
 int launch_prepack_outliers(const uint32_t* q, const uint16_t* lut, const int32_t* off, const uint16_t* ccols,
                             const uint8_t* cvals, int N, int K, int wpr, int group_size, int goff, int ngroups,
