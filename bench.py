@@ -1002,6 +1002,73 @@ def run_case(args):
                       "TFLOP/s": round(2.0 * M * N * K / ms / 1e9, 1)}))
 
 
+def _load_by_path(name, rel):
+    """A module of this repository loaded from its file, without importing
+    its package (whose import loads libwlq_b200.so)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, rel))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_vllm_decode(args):
+    """BASELINE config 3 inside vLLM, one plugin per process: a random-init
+    Qwen2.5-7B-shaped model in the reference's on-disk format (per-row
+    codebooks, the only layout the reference reads; DoRA rank 16 per
+    projection, 0.5% outliers), batch 32 x (1024 prompt + 256 generated)
+    tokens, decode as full CUDA graphs.  --vllm-decode ours: this package's
+    quantisation method; reference: the unmodified reference plugin installed
+    in baseline/_ref (its kernels JIT-compiled from compute_90 PTX), with this
+    package never imported.  Prints one JSON line."""
+    os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
+    ck = _load_by_path("_wlq_checkpoint", "qwen_wlqfastshot_helen_beta_b200/checkpoint.py")
+    model = args.model
+    if not os.path.isfile(os.path.join(model, "config.json")):
+        t0 = time.time()
+        ck.write_checkpoint(model, num_layers=args.layers, group_size=0, seed=0)
+        print(f"checkpoint written in {time.time() - t0:.0f} s", file=sys.stderr, flush=True)
+    if args.vllm_decode == "reference":
+        ref = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref, "vllm_wlq")):
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref/vllm_wlq is not installed"}))
+            return
+        sys.path.insert(0, ref)
+        import vllm_wlq
+        vllm_wlq.register()
+    else:
+        from qwen_wlqfastshot_helen_beta_b200 import register
+        register()
+    from vllm import LLM, SamplingParams
+    batch, prompt, gen = 32, 1024, 256
+    llm = LLM(model=model, dtype="bfloat16", skip_tokenizer_init=True, seed=0, max_model_len=prompt + gen + 16,
+              max_num_seqs=batch, gpu_memory_utilization=0.80, enable_prefix_caching=False,
+              compilation_config={"mode": 0, "cudagraph_mode": "FULL_DECODE_ONLY"})
+    with open(os.path.join(model, "config.json")) as f:
+        vocab = json.load(f)["vocab_size"]
+    rng = np.random.default_rng(0)
+    prompts = [{"prompt_token_ids": rng.integers(0, vocab, size=prompt).tolist()} for _ in range(batch)]
+
+    def run(n):
+        sp = SamplingParams(max_tokens=n, min_tokens=n, ignore_eos=True, temperature=0.0, detokenize=False)
+        t = time.perf_counter()
+        outs = llm.generate(prompts, sp, use_tqdm=False)
+        return time.perf_counter() - t, sum(len(o.outputs[0].token_ids) for o in outs), outs
+
+    run(4)  # warm-up
+    t1, _, _ = run(1)
+    tg, ntok, outs = run(gen)
+    first = [list(o.outputs[0].token_ids[:8]) for o in outs[:2]]
+    print(json.dumps({
+        "impl": args.vllm_decode, "metric": "Qwen2.5-7B decode tok/s (vLLM, every linear WLQ)",
+        "value": round(ntok / tg, 1), "unit": "tok/s", "decode_tok_s": round(batch * (gen - 1) / max(tg - t1, 1e-9), 1),
+        "prefill_s": round(t1, 3), "generate_s": round(tg, 3), "tokens": ntok, "first_tokens": first,
+        "config": {"model": "random-init Qwen2.5-7B shape, per-row codebooks, rank 16, 0.5% outliers",
+                   "layers": args.layers or 28, "batch": batch, "prompt": prompt, "gen": gen, "dtype": "bf16",
+                   "parallelism": "single", "cudagraph_mode": "FULL_DECODE_ONLY", "compile": "off"},
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="name:M (M <= 16: GEMV; larger: GEMM), one configuration for "
@@ -1015,7 +1082,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-baselines", action="store_true", help="skip the config-0 CPU leg and the reference's GPU "
                     "kernels leg")
+    ap.add_argument("--vllm-decode", choices=["ours", "reference"], default=None,
+                    help="BASELINE config 3 in vLLM with this package's or the reference's plugin")
+    ap.add_argument("--model", default="/tmp/wlq_qwen7b_rowlut", help="checkpoint directory for --vllm-decode")
+    ap.add_argument("--layers", type=int, default=None, help="layer count of the --vllm-decode model (28)")
     args = ap.parse_args()
+    if args.vllm_decode:
+        run_vllm_decode(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.case:
