@@ -13,19 +13,26 @@ L2; no flush needed).
 
 Metric: algorithmic bytes (indices, codebooks, outlier CSR, DoRA tensors,
 activations, outputs) / time, in GB/s, whole job.  ``value`` times K steps of
-a CUDA graph of the step with inputs resident in HBM; ``roofline`` divides the
-same bytes by the summed kernel-only durations (CUDA events recorded between
-the kernels inside the graph) and by the measured HBM copy bandwidth; ``e2e``
-times K steps through the public op with host (pinned) activations copied in
-and outputs copied out every step.
+a CUDA graph of the step with inputs resident in HBM; ``roofline`` divides
+this GPU's bytes per step by the same graph's time per step (kernel time per
+step <= ms_per_step) and by the measured HBM copy bandwidth, with per-launch
+figures from a second graph that has an event pair around every launch;
+``e2e`` times K steps through the public op with host (pinned) activations
+copied in and outputs copied out every step.  Sub-objects: ``gemm`` (BASELINE
+config 2, the prefill op), ``cpu_baseline`` and ``cpu_baseline_config0``
+(the reference's CPU steps; BASELINE config 0 beside this package's op),
+``reference_gpu_baseline`` (the reference's own CUDA kernels on this GPU).
 
 With --gpus N > 1 (torchrun, one rank per GPU) the linears are sharded the way
 vLLM tensor parallelism shards them (qkv/gate_up by output rows, o/down by
-input columns, the latter followed by an NCCL all-reduce of [M, hidden]);
-value = bytes of the whole layer / max-over-ranks time (strong scaling).
+input columns, the latter followed by the all-reduce of [M, hidden]: fused
+into the decode GEMV, NCCL after the prefill GEMM); value = bytes of the
+whole layer / max-over-ranks time (strong scaling); ``tp_allreduce`` gives
+per-call times of the row-parallel layers with and without the fusion.
 
 --impl reference times the reference's CPU dequantize-then-matmul path
 (oracle/cpu_baseline.py) on the host cores on the same workload and metric.
+--vllm-decode ours|reference runs BASELINE config 3 inside vLLM.
 """
 from __future__ import annotations
 
@@ -451,6 +458,7 @@ def run_ours(args):
     eager_value = step_bytes_job * args.steps / (eager_ms * 1e-3) / 1e9
 
     gemm = gemm_leg(layers, dev, launch_gemm, peaks, peaks_kind, local, world, rank)
+    tp_detail = tp_allreduce_leg(per_copy[0], comm, launch, dev, world) if world > 1 else None
     config0 = ref_gpu = None
     if world == 1 and not args.no_baselines:
         config0 = cpu_baseline_config0(dev, args.cpu_budget)
@@ -508,6 +516,8 @@ def run_ours(args):
         }
         if gemm is not None:
             result["gemm"] = gemm
+        if tp_detail is not None:
+            result["tp_allreduce"] = tp_detail
         if config0 is not None:
             result["cpu_baseline_config0"] = config0
         if ref_gpu is not None:
@@ -523,6 +533,48 @@ def run_ours(args):
                 raise RuntimeError("fused all-reduce: a rank timed out waiting for another")
         dist.destroy_process_group()
     return result, layers if rank == 0 else None
+
+
+def tp_allreduce_leg(calls, comm, launch, dev, world, reps=20):
+    """Per-call time of the row-parallel decode layers (o, down) at M = 1 and
+    16 on this rank's K shard: the GEMV alone, the GEMV followed by vLLM's
+    NCCL all-reduce of [M, N], and the GEMV with the all-reduce fused
+    (wlq_gemv_allreduce); graphs of `reps` calls, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    out = {}
+    for (_, name, M, L, x, a, y) in calls:
+        if name not in ("o", "down") or M not in (1, 16):
+            continue
+        variants = {"gemv_alone": lambda: launch(L, x, a, y),
+                    "gemv_then_nccl": lambda: (launch(L, x, a, y), dist.all_reduce(y)),
+                    "fused": lambda: launch(L, x, a, y, name)}
+        row = {}
+        for key, fn in variants.items():
+            fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    for _ in range(reps):
+                        fn()
+            torch.cuda.current_stream().wait_stream(s)
+            g.replay()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / reps * 1e3], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            row[key + "_us"] = round(float(t[0]), 2)
+            del g
+        out[f"{name}/M{M}"] = row
+    return {"unit": "us per call, max over ranks", "shard": f"K / {world} per rank", "per_config": out}
 
 
 def gemm_leg(layers, dev, launch, peaks, peaks_kind, local, world=1, rank=0, reps=10, warmup=3):
