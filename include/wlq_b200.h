@@ -214,7 +214,12 @@ WLQ_API int wlq_init_workspaces(int64_t max_N, int64_t max_K, int device);
  * allocates one buffer of
  * wlq_tp_buffer_bytes(world, max_N) with wlq_tp_buffer_alloc, exchanges the
  * 64-byte IPC handles with the other ranks (any host channel) and maps theirs
- * with wlq_tp_buffer_open.  All ranks must issue the same sequence of calls.
+ * with wlq_tp_buffer_open.  All ranks must issue the same sequence of calls,
+ * on one stream per rank, one call after another: the per-tile epoch
+ * counters and the value slots of a buffer are shared by every call made
+ * with it (o and down alike), so two calls in flight at once on one rank
+ * (concurrent streams, or a call overlapping the previous one through
+ * programmatic dependent launch) race; use one buffer set per stream.
  * No reference counterpart: the reference leaves the all-reduce to vLLM's
  * NCCL call after the layer (vllm: model_executor/layers/linear.py:1558-1559). */
 WLQ_API size_t wlq_tp_buffer_bytes(int world, int max_N);
