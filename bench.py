@@ -1029,15 +1029,17 @@ def run_case(args):
     gen = torch.Generator(device="cuda")
     gen.manual_seed(5)
     x = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)
-    hs = [S.lora_h(L, x) for L in layers]
     out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    import qwen_wlqfastshot_helen_beta_b200  # noqa: F401  (torch ops)
 
-    def call(i):  # decode: h = A x inside the GEMV; prefill: h given
+    def call(i):  # the op as apply() runs it: decode folds h = A x, prefill runs wlq_lora_h + the GEMM
         L = layers[i % len(layers)]
         if M <= 16:
             S.forward_fold(L, x, out)
         else:
-            S.forward(L, x, out, hs[i % len(layers)])
+            torch.ops.wlq_fastShot.gemm(x, L.q_packed, L.lut_packed, out, N, K, 4, L.words_per_row, L.chunk_offsets,
+                                        L.cols_packed, L.delta_packed, None, L.lora_B, L.dora_gamma, L.lora_scale,
+                                        GROUP, 0, 1, L.lora_A_act)
 
     for i in range(args.warmup):
         call(i)
