@@ -79,6 +79,23 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool o
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0)
                  : "memory");
 }
+// The same with the byte count given (16, or 0 to zero-fill): a lane whose
+// count is fixed for a whole loop keeps it in a register.
+__device__ __forceinline__ void cp_async16_n(uint32_t dst, const void* src, uint32_t n) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+// base + i * stride as one wide multiply-add (the FMA pipe, not the
+// integer/logic pipe that the lookups keep busy).
+__device__ __forceinline__ const void* ptr_mad(const void* base, uint32_t i, uint32_t stride) {
+    uint64_t d;
+    asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(d) : "r"(i), "r"(stride), "l"(reinterpret_cast<uint64_t>(base)));
+    return reinterpret_cast<const void*>(d);
+}
+__device__ __forceinline__ uint32_t mad_u32(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -88,6 +105,21 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
     uint4 r;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a)
                  : "memory");
+    return r;
+}
+// ... at a constant byte offset, folded into the instruction's address
+template <int OFF>
+__device__ __forceinline__ uint4 lds128_at(uint32_t a) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "r"(a), "n"(OFF) : "memory");
+    return r;
+}
+template <int OFF>
+__device__ __forceinline__ uint4 ldg_keep_v4_at(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::evict_last.v4.u32 {%0,%1,%2,%3}, [%4+%5];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "n"(OFF));
     return r;
 }
 

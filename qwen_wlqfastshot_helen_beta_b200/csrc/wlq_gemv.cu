@@ -88,9 +88,21 @@ int dispatch32(const GemvParams& p, bool xsmem, int ctas, int cs, cudaStream_t s
     }
 }
 
+// one 16-warp CTA per SM with the activations staged: prepacked layout,
+// 16-byte aligned rows, at most 16 tokens
+template <typename T, int NT>
+int dispatch_big(const GemvParams& p, int ctas, int cs, cudaStream_t stream, int* fit) {
+    switch (codebook_slots(p.G)) {
+        case 0: return launch_variant<T, NT, 0, true, true, true, 0, kBigStages, kBigWarps>(p, ctas, cs, stream, fit);
+        case 2: return launch_variant<T, NT, 2, true, true, true, 0, kBigStages, kBigWarps>(p, ctas, cs, stream, fit);
+        default: return launch_variant<T, NT, 4, true, true, true, 0, kBigStages, kBigWarps>(p, ctas, cs, stream, fit);
+    }
+}
+
 template <typename T>
-int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int ctas, int cs, cudaStream_t stream,
-             int* fit) {
+int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, bool big, int ctas, int cs,
+             cudaStream_t stream, int* fit) {
+    if (big) return p.M <= 8 ? dispatch_big<T, 1>(p, ctas, cs, stream, fit) : dispatch_big<T, 2>(p, ctas, cs, stream, fit);
     if (p.M > 16) return dispatch32<T>(p, xsmem, ctas, cs, stream, fit);
     return p.M <= 8 ? dispatch_slots<T, 1>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit)
                     : dispatch_slots<T, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit);
@@ -101,6 +113,7 @@ int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, int cta
 struct Plan {
     int cs;
     bool xsmem, stages2;
+    bool big;  // one 16-warp CTA per SM (kBigWarps) instead of 4-warp CTAs
 };
 
 struct FitKey {
@@ -199,23 +212,36 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     }
     const bool bf16 = a.dtype == WLQ_DTYPE_BF16;
     const int tiles = (a.N + kRowsPerTile - 1) / kRowsPerTile;
-    const int ctas = (tiles + kWarps - 1) / kWarps;
+    const int ctas4 = (tiles + kWarps - 1) / kWarps;
+    const int ctas16 = (tiles + kBigWarps - 1) / kBigWarps;
     const int slots = codebook_slots(p.G);
     // r <= 48 (rt = 3) always runs a 2-stage ring: three stages of its larger
     // A blocks would leave no room for 4 CTAs per SM
     const int stages = rt == 3 ? 2 : kStages;
     const int ring_bytes = kWarps * stages * ring_stage_bytes(slots, rt);
+    // one 16-warp CTA per SM: prepacked layout, 16-byte aligned rows, at most
+    // 16 tokens and r <= 32
+    const bool big_ok = a.lut_prepacked && xvec && a.M <= 16 && rt <= 2;
+    const size_t big_fixed = (size_t)kBigWarps * kBigStages * ring_stage_bytes(slots, rt) +
+                             gemv_static_smem(a.M <= 8 ? 1 : 2, kBigWarps);
 
-    auto configure = [&](int cs) {
+    auto configure = [&](int cs, bool big) {
         Plan pl;
         pl.cs = cs;
+        pl.big = big;
         p.chunks_per_rank = (p.kchunks + cs - 1) / cs;
         p.x_stride = p.chunks_per_rank * kChunk + 8;
+        const int64_t x_bytes = ((int64_t)a.M * p.x_stride * 2 + 127) / 128 * 128;
+        if (big) {  // the activations must fit beside the 16 rings
+            pl.xsmem = (size_t)x_bytes + big_fixed <= kMaxBlockSmem;
+            pl.stages2 = false;
+            p.x_bytes = pl.xsmem ? (int)x_bytes : 0;
+            return pl;
+        }
         // stage the rank's activations in shared memory when 4 CTAs per SM
         // still fit beside the rings; larger slices are read through L1.
         // Computing h (larger stages) for 9..16 tokens, a 2-stage ring when
         // that lets the activations be staged.
-        const int64_t x_bytes = ((int64_t)a.M * p.x_stride * 2 + 127) / 128 * 128;
         pl.xsmem = x_bytes + ring_bytes <= 48 * 1024;
         pl.stages2 = rt == 3 ||
                      (rt > 0 && a.M > 8 && !pl.xsmem && x_bytes + ring_bytes / kStages * 2 <= 48 * 1024);
@@ -224,48 +250,71 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
         return pl;
     };
     auto run = [&](const Plan& pl, int* fit) {
-        if (rt > 0) return launch_fold(p, rt, bf16, pl.xsmem, pl.stages2, ctas, pl.cs, stream, fit);
-        return bf16 ? dispatch<__nv_bfloat16>(p, a.lut_prepacked, xvec, pl.xsmem, ctas, pl.cs, stream, fit)
-                    : dispatch<__half>(p, a.lut_prepacked, xvec, pl.xsmem, ctas, pl.cs, stream, fit);
+        const int ctas = pl.big ? ctas16 : ctas4;
+        if (rt > 0) return launch_fold(p, rt, bf16, pl.xsmem, pl.stages2, pl.big, ctas, pl.cs, stream, fit);
+        return bf16 ? dispatch<__nv_bfloat16>(p, a.lut_prepacked, xvec, pl.xsmem, pl.big, ctas, pl.cs, stream, fit)
+                    : dispatch<__half>(p, a.lut_prepacked, xvec, pl.xsmem, pl.big, ctas, pl.cs, stream, fit);
     };
 
-    // Split K over a cluster (up to 16 CTAs) until about 4 CTAs (16 warps)
-    // per SM are in flight, keeping at least 2 chunks per rank, and at least 4
-    // above 8 ranks (measured: a 14-way split of 28 chunks lost to the wider
-    // reduction, a 16-way split of 148 won 15 %); then take the largest split
-    // (down to none) whose clusters the device holds in one wave.  A split
+    // Split K over a cluster (up to 16 CTAs) until about 16 warps per SM are
+    // in flight (4 CTAs of 4 warps, or one of 16), keeping at least 2 chunks
+    // per rank, and at least 4 above 8 ranks (measured: a 14-way split of 28
+    // chunks lost to the wider reduction, a 16-way split of 148 won 15 %);
+    // then take the largest split (down to none) whose clusters the device
+    // holds in one wave.  4-warp CTAs first; where their activations would
+    // have to come through L1, 16-warp CTAs that stage them instead.  A split
     // forced through wlq_gemv_set_split replaces the choice.
     const int forced = g_forced_split.load(std::memory_order_relaxed);
-    Plan pl = configure(1);
-    if (forced > 0) {
-        if (forced > kMaxSplit || forced > p.kchunks)
-            return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: forced split %d needs 1..%d and at most %d chunks of 128 "
-                        "columns", forced, kMaxSplit, p.kchunks);
-        pl = configure(forced);
-    } else {
-        const int sms = device_sm_count();
-        auto chunks_ok = [&](int cs) { return p.kchunks >= (cs > 8 ? 4 : 2) * cs; };
+    const int sms = device_sm_count();
+    auto chunks_ok = [&](int cs) { return p.kchunks >= (cs > 8 ? 4 : 2) * cs; };
+    auto search = [&](bool big, Plan& out) {
+        const int ctas = big ? ctas16 : ctas4;
+        const int64_t target = big ? (int64_t)sms : 4LL * sms;
         int cs_max = 1;
-        while (cs_max < kMaxSplit && (int64_t)ctas * cs_max < 4LL * sms && chunks_ok(cs_max + 1)) ++cs_max;
+        while (cs_max < kMaxSplit && (int64_t)ctas * cs_max < target && chunks_ok(cs_max + 1)) ++cs_max;
+        out = configure(1, big);
         for (int cs = cs_max; cs > 1; --cs) {
-            const Plan c = configure(cs);
+            const Plan c = configure(cs, big);
+            if (big && !c.xsmem) continue;
             int fit = 0;
             const int rc = run(c, &fit);  // a refused non-portable size reports fit = 0 (cached)
             if (rc) return rc;
             if (ctas <= fit) {
-                pl = c;
+                out = c;
                 break;
             }
         }
+        return (int)WLQ_OK;
+    };
+    Plan pl;
+    if (forced > 0) {
+        if (forced > kMaxSplit || forced > p.kchunks)
+            return fail(WLQ_ERR_INVALID_ARG, "wlq_gemv: forced split %d needs 1..%d and at most %d chunks of 128 "
+                        "columns", forced, kMaxSplit, p.kchunks);
+        pl = configure(forced, false);
+        if (!pl.xsmem && big_ok) {
+            const Plan b = configure(forced, true);
+            if (b.xsmem) pl = b;
+        }
+    } else {
+        int rc = search(false, pl);
+        if (rc) return rc;
+        if (!pl.xsmem && big_ok) {
+            Plan b;
+            rc = search(true, b);
+            if (rc) return rc;
+            if (b.xsmem) pl = b;
+        }
     }
-    configure(pl.cs);
+    configure(pl.cs, pl.big);
     int rc = run(pl, nullptr);
     if (rc == kRetryPortable && forced == 0) {
         // the launch refused a non-portable cluster size: once more at 8 CTAs
-        // or fewer
+        // or fewer (4-warp CTAs when the 16-warp ones cannot stage that slice)
         int cs = pl.cs > 8 ? 8 : pl.cs;
         while (cs > 1 && p.kchunks < 2 * cs) --cs;
-        pl = configure(cs);
+        pl = configure(cs, pl.big);
+        if (pl.big && !pl.xsmem) pl = configure(cs, false);
         rc = run(pl, nullptr);
     }
     if (rc == kRetryPortable)

@@ -14,8 +14,11 @@ namespace gemv {
 namespace {
 
 template <typename T, int NT, int NSLOT>
-int fold_x(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int cs, cudaStream_t stream,
+int fold_x(const GemvParams& p, int rt, bool xsmem, bool stages2, bool big, int ctas, int cs, cudaStream_t stream,
            int* fit) {
+    if (big)  // one 16-warp CTA per SM, activations staged (r <= 32)
+        return rt == 1 ? launch_variant<T, NT, NSLOT, true, true, true, 1, kBigStages, kBigWarps>(p, ctas, cs, stream, fit)
+                       : launch_variant<T, NT, NSLOT, true, true, true, 2, kBigStages, kBigWarps>(p, ctas, cs, stream, fit);
     if (rt == 3)  // r <= 48 (a fused qkv of three rank-16 adapters): always a 2-stage ring
         return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 3, 2>(p, ctas, cs, stream, fit)
                      : launch_variant<T, NT, NSLOT, true, true, false, 3, 2>(p, ctas, cs, stream, fit);
@@ -32,12 +35,12 @@ int fold_x(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int 
 }
 
 template <typename T, int NT>
-int fold_slots(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int cs, cudaStream_t stream,
-               int* fit) {
+int fold_slots(const GemvParams& p, int rt, bool xsmem, bool stages2, bool big, int ctas, int cs,
+               cudaStream_t stream, int* fit) {
     switch (codebook_slots(p.G)) {
-        case 0: return fold_x<T, NT, 0>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
-        case 2: return fold_x<T, NT, 2>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
-        default: return fold_x<T, NT, 4>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
+        case 0: return fold_x<T, NT, 0>(p, rt, xsmem, stages2, big, ctas, cs, stream, fit);
+        case 2: return fold_x<T, NT, 2>(p, rt, xsmem, stages2, big, ctas, cs, stream, fit);
+        default: return fold_x<T, NT, 4>(p, rt, xsmem, stages2, big, ctas, cs, stream, fit);
     }
 }
 
@@ -58,19 +61,19 @@ int fold32(const GemvParams& p, bool xsmem, int ctas, int cs, cudaStream_t strea
 }
 
 template <typename T>
-int fold_tokens(const GemvParams& p, int rt, bool xsmem, bool stages2, int ctas, int cs, cudaStream_t stream,
-                int* fit) {
+int fold_tokens(const GemvParams& p, int rt, bool xsmem, bool stages2, bool big, int ctas, int cs,
+                cudaStream_t stream, int* fit) {
     if (p.M > 16) return fold32<T>(p, xsmem, ctas, cs, stream, fit);
-    return p.M <= 8 ? fold_slots<T, 1>(p, rt, xsmem, false, ctas, cs, stream, fit)
-                    : fold_slots<T, 2>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
+    return p.M <= 8 ? fold_slots<T, 1>(p, rt, xsmem, false, big, ctas, cs, stream, fit)
+                    : fold_slots<T, 2>(p, rt, xsmem, stages2, big, ctas, cs, stream, fit);
 }
 
 }  // namespace
 
-int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, bool stages2, int ctas, int cs,
+int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, bool stages2, bool big, int ctas, int cs,
                 cudaStream_t stream, int* fit) {
-    return bf16 ? fold_tokens<__nv_bfloat16>(p, rt, xsmem, stages2, ctas, cs, stream, fit)
-                : fold_tokens<__half>(p, rt, xsmem, stages2, ctas, cs, stream, fit);
+    return bf16 ? fold_tokens<__nv_bfloat16>(p, rt, xsmem, stages2, big, ctas, cs, stream, fit)
+                : fold_tokens<__half>(p, rt, xsmem, stages2, big, ctas, cs, stream, fit);
 }
 
 }  // namespace gemv

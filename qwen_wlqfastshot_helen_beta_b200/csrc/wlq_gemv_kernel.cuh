@@ -17,6 +17,9 @@ constexpr int kMaxTp = 8;    // ranks of a fused all-reduce
 constexpr int kMaxGemvM = 32;  // token rows of one launch: 1, 2 or 4 eight-token MMA tiles
 constexpr int kMaxSplit = 16;  // CTAs of a K-split cluster (above 8: a non-portable cluster size)
 
+// compile-time flag for generic lambdas
+template <bool B> struct BoolTag { static constexpr bool value = B; };
+
 struct GemvParams {
     const uint32_t* q;
     const uint16_t* lut;
@@ -54,6 +57,14 @@ __device__ __forceinline__ float codebook_value(const uint16_t* __restrict__ lut
         return ActTraits<T>::bits_to_f32(bits);
     }
     return ActTraits<T>::bits_to_f32(ActTraits<T>::from_f16_bits(__ldg(lut + entry * 16 + q)));
+}
+
+// An 8-column activation piece at a constant byte offset from a chunk's
+// base: shared memory (staged) or global through L1.
+template <bool XSMEM, int OFF>
+__device__ __forceinline__ uint4 x8_at(uint32_t sa, const uint16_t* gp) {
+    if constexpr (XSMEM) return lds128_at<OFF>(sa);
+    else return ldg_keep_v4_at<OFF>(gp);
 }
 
 // Issues the staging of x[0:M, kb:kb+cols) into shared memory as one
@@ -198,22 +209,29 @@ __device__ void tp_allreduce_tile(const GemvParams& p, float (*part)[MT], uint32
 // h meet in shared memory and each warp adds s B h for its rows.  With the K
 // range split over a cluster each rank adds the term for its own range, and
 // the split-K reduction sums them.
-template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int S, int RT>
-__global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p) {
+template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int S, int RT, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_kernel(const GemvParams p) {
     constexpr bool GROUPED = NSLOT > 0;
     constexpr int MT = 8 * NT;
     using R = Ring<NSLOT, RT>;
     static_assert(S >= 2, "ring needs two stages");
     static_assert(RT == 0 || XVEC, "h = A x in the kernel needs 16-byte aligned rows");
     static_assert(S * R::kStageBytes >= RT * 16 * MT * 4, "the partial h reuses the ring");
-    extern __shared__ __align__(128) uint8_t smem[];  // [x stage (XSMEM)][kWarps][S] ring stages
-    __shared__ float part[kWarps][kRowsPerTile][MT];  // per-warp partial tile
+    static_assert(WARPS == 4 || WARPS == 16, "4 warps (4 CTAs per SM) or 16 (one CTA per SM)");
+    extern __shared__ __align__(128) uint8_t smem[];  // [x stage (XSMEM)][WARPS][S] ring stages
+    __shared__ float part[WARPS][kRowsPerTile][MT];   // per-warp partial tile
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2;
     const int t = lane & 3;
-    const int tile_row0 = (blockIdx.x * kWarps + warp) * kRowsPerTile;
+    const int tile_row0 = (blockIdx.x * WARPS + warp) * kRowsPerTile;
+    // computing h = A x: every chunk's 128 columns are split into four
+    // 32-column blocks; warp w takes block w % 4 of the chunks whose offset
+    // in the CTA's range is w / 4 modulo WARPS / 4 (every chunk with 4 warps)
+    constexpr int kHPhases = WARPS / 4;
+    const int hblk = warp & 3, hphase = warp >> 2;
+    auto h_duty = [&](int c) { return kHPhases == 1 || (c - blockIdx.y * p.chunks_per_rank) % kHPhases == hphase; };
     const int row0 = tile_row0 + g;
     const bool v0 = row0 < p.N;
     const bool v1 = row0 + 8 < p.N;
@@ -235,34 +253,46 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 
     // The lane's part of every ring copy is fixed for the whole K range: the
     // 16-byte piece q4 = lane % 4 of index rows lane / 4 and lane / 4 + 8, its
-    // codebook slot and half, and (computing h) its rows of A.  Their element
-    // offsets from the tensors' starts are computed once, so a chunk only adds
-    // its stride.
+    // codebook slot and half, and (computing h) its rows of A.  Their sources
+    // at chunk 0 and their byte counts (16, or 0 to zero-fill a row past N or
+    // a rank past r) are set once; a chunk inside K then costs one wide
+    // multiply-add per copy and no integer/logic instruction.  Chunks past
+    // c_full (a ragged K end) take the checked path.
     const int q4 = lane & 3;
     const int ir = lane >> 2;
+    const int c_full = p.K / kChunk;
     const bool iok0 = tile_row0 + ir < p.N, iok1 = tile_row0 + ir + 8 < p.N;
     const uint32_t ioff0 = iok0 ? (uint32_t)(tile_row0 + ir) * (uint32_t)p.wpr + 4u * q4 : 0u;
     const uint32_t ioff1 = iok1 ? (uint32_t)(tile_row0 + ir + 8) * (uint32_t)p.wpr + 4u * q4 : 0u;
+    const uint32_t qn0 = iok0 ? 16u : 0u, qn1 = iok1 ? 16u : 0u;
     const uint32_t idst = (uint32_t)(ir * 64 + q4 * 16);
     constexpr int kSlots = GROUPED ? NSLOT : 1;
     const int ls = (lane >> 1) % kSlots, lhalf = lane & 1;  // codebook slot and half of this lane
+    // groups at most a chunk wide: chunk c's first group is c * (128 / G) +
+    // goff / G and the chunk spans the same number of groups every time
+    const bool cb_fixed = GROUPED && p.G <= kChunk;
+    const uint32_t cb_step = cb_fixed ? (uint32_t)(kChunk >> p.log2G) * 32u : 0u;  // codebook bytes per chunk
+    const int cb_used = cb_fixed ? (kChunk >> p.log2G) + ((p.goff & (p.G - 1)) != 0 ? 1 : 0) : 0;
     bool lok[kSlots];
-    uint32_t loff[kSlots], ldst[kSlots];
+    uint32_t loff[kSlots], ldst[kSlots], lnf[kSlots];
 #pragma unroll
     for (int i = 0; i < kSlots; ++i) {
         const int r = (lane + 32 * i) / (2 * kSlots);
         lok[i] = tile_row0 + r < p.N;
         loff[i] = lok[i] ? ((uint32_t)(tile_row0 + r) * (uint32_t)p.ngroups + ls) * 16u + 8u * lhalf : 0u;
         ldst[i] = (uint32_t)(R::kIdxBytes + (r * kSlots + ls) * 32 + lhalf * 16);
+        lnf[i] = lok[i] && ls < cb_used ? 16u : 0u;
     }
+    const uint16_t* lbase = p.lut + (cb_fixed ? (uint32_t)(p.goff >> p.log2G) * 16u : 0u);
     constexpr int kAPieces = RT > 0 ? 2 * RT : 1;
-    uint32_t aoff[kAPieces];
+    uint32_t aoff[kAPieces], an[kAPieces];
     bool aok[kAPieces];
 #pragma unroll
     for (int i = 0; i < kAPieces; ++i) {
         const int ar = ir + 8 * i;
         aok[i] = RT > 0 && ar < p.r;
-        aoff[i] = aok[i] ? (uint32_t)ar * (uint32_t)p.K + 32u * warp + 8u * q4 : 0u;
+        aoff[i] = aok[i] ? (uint32_t)ar * (uint32_t)p.K + 32u * hblk + 8u * q4 : 0u;
+        an[i] = aok[i] ? 16u : 0u;
     }
 
     // chunk c into ring stage st; one commit group per lane per chunk, empty
@@ -270,31 +300,58 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
     auto issue = [&](int c, int st) {
         if (c < c_end) {
             const uint32_t base = ring + (uint32_t)(st * R::kStageBytes);
-            const uint32_t wi = (uint32_t)c * (kChunk / 8);  // first index word of the chunk
-            const bool wok = (int)(wi + 4u * q4) < p.wpr;
-            const bool ok0 = iok0 && wok, ok1 = iok1 && wok;
-            cp_async16(base + idst, p.q + (ok0 ? ioff0 + wi : 0u), ok0);
-            cp_async16(base + idst + 8 * 64, p.q + (ok1 ? ioff1 + wi : 0u), ok1);
-            if constexpr (GROUPED) {
-                const int g0 = group_at(c * kChunk);
-                const int used = group_at(c * kChunk + kChunk - 1) - g0 + 1;
-                const bool sok = ls < used;
+            const uint32_t cu = (uint32_t)c;
+            if (c < c_full) {
+                cp_async16_n(base + idst, ptr_mad(p.q + ioff0, cu, 64u), qn0);
+                cp_async16_n(base + idst + 8 * 64, ptr_mad(p.q + ioff1, cu, 64u), qn1);
+                if constexpr (GROUPED) {
+                    if (cb_fixed) {
 #pragma unroll
-                for (int i = 0; i < NSLOT; ++i) {
-                    const bool ok = lok[i] && sok;
-                    cp_async16(base + ldst[i], p.lut + (ok ? loff[i] + (uint32_t)g0 * 16u : 0u), ok);
+                        for (int i = 0; i < NSLOT; ++i)
+                            cp_async16_n(base + ldst[i], ptr_mad(lbase + loff[i], cu, cb_step), lnf[i]);
+                    } else {
+                        const int g0 = (c * kChunk + p.goff) >> p.log2G;
+                        const int used = ((c * kChunk + kChunk - 1 + p.goff) >> p.log2G) - g0 + 1;
+#pragma unroll
+                        for (int i = 0; i < NSLOT; ++i)
+                            cp_async16_n(base + ldst[i], ptr_mad(p.lut + loff[i], (uint32_t)g0, 32u),
+                                         lok[i] && ls < used ? 16u : 0u);
+                    }
                 }
-            }
-            if constexpr (RT > 0) {
-                // rows [0, 16 RT) of A, columns [128c + 32w, +32); rows past r
-                // and columns past K (K % 8 == 0) read as zero
-                const uint32_t ca = (uint32_t)c * kChunk;
-                const bool cok = (int)(ca + 32u * warp + 8u * q4) < p.K;
+                if (RT > 0 && h_duty(c)) {
 #pragma unroll
-                for (int i = 0; i < 2 * RT; ++i) {
-                    const bool ok = aok[i] && cok;
-                    cp_async16(base + R::kIdxBytes + R::kPlaneBytes + (ir + 8 * i) * 64 + q4 * 16,
-                               p.loraA + (ok ? aoff[i] + ca : 0u), ok);
+                    for (int i = 0; i < 2 * RT; ++i)
+                        cp_async16_n(base + R::kIdxBytes + R::kPlaneBytes + (ir + 8 * i) * 64 + q4 * 16,
+                                     ptr_mad(p.loraA + aoff[i], cu, 2u * kChunk), an[i]);
+                }
+            } else {
+                const uint32_t wi = cu * (kChunk / 8);  // first index word of the chunk
+                const bool wok = (int)(wi + 4u * q4) < p.wpr;
+                const bool ok0 = iok0 && wok, ok1 = iok1 && wok;
+                cp_async16(base + idst, p.q + (ok0 ? ioff0 + wi : 0u), ok0);
+                cp_async16(base + idst + 8 * 64, p.q + (ok1 ? ioff1 + wi : 0u), ok1);
+                if constexpr (GROUPED) {
+                    const int g0 = group_at(c * kChunk);
+                    const int used = group_at(c * kChunk + kChunk - 1) - g0 + 1;
+                    const bool sok = ls < used;
+#pragma unroll
+                    for (int i = 0; i < NSLOT; ++i) {
+                        const bool ok = lok[i] && sok;
+                        cp_async16(base + ldst[i], p.lut + (ok ? loff[i] + (uint32_t)g0 * 16u : 0u), ok);
+                    }
+                }
+                if (RT > 0 && h_duty(c)) {
+                    // rows [0, 16 RT) of A, columns [128c + 32b, +32) of this
+                    // warp's block b; rows past r and columns past K (K % 8
+                    // == 0) read as zero
+                    const uint32_t ca = cu * kChunk;
+                    const bool cok = (int)(ca + 32u * hblk + 8u * q4) < p.K;
+#pragma unroll
+                    for (int i = 0; i < 2 * RT; ++i) {
+                        const bool ok = aok[i] && cok;
+                        cp_async16(base + R::kIdxBytes + R::kPlaneBytes + (ir + 8 * i) * 64 + q4 * 16,
+                                   p.loraA + (ok ? aoff[i] + ca : 0u), ok);
+                    }
                 }
             }
         }
@@ -502,24 +559,55 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt) xnext[tt] = c_begin < c_end ? lds_x8(tt, 0) : make_uint4(0u, 0u, 0u, 0u);
 
-    int st = 0;
-    for (int c = c_begin; c < c_end; ++c) {
-        cp_async_wait<S - 2>();  // this lane's copies of chunk c have landed
-        __syncwarp();            // ... and every lane's; the previous stage is free
-        issue(c + S - 1, st == 0 ? S - 1 : st - 1);
-        const uint32_t base = ring + (uint32_t)(st * R::kStageBytes);
-        st = st + 1 == S ? 0 : st + 1;
+    // Unchecked activation sources for chunks inside K (16-byte aligned
+    // rows): token rows past M read token 0's row, whose products land only
+    // in output columns that are never stored.  Shared-memory addresses
+    // (XSMEM) or global pointers of this lane's 8-column pieces at chunk
+    // c_begin: the lookup's (columns 32t..) and the h MMA's (32w + 8t).
+    uint32_t xsa[NT], xfa[NT];
+    const uint16_t* xga[NT];
+    const uint16_t* xgf[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int tok = 8 * j + g < p.M ? 8 * j + g : 0;
+        xsa[j] = XSMEM ? smem_u32(xs + tok * p.x_stride + 32 * t) : 0u;
+        xfa[j] = XSMEM ? smem_u32(xs + tok * p.x_stride + 32 * hblk + 8 * t) : 0u;
+        xga[j] = reinterpret_cast<const uint16_t*>(x) + (int64_t)tok * p.K + kb0 + 32 * t;
+        xgf[j] = reinterpret_cast<const uint16_t*>(x) + (int64_t)tok * p.K + kb0 + 32 * hblk + 8 * t;
+    }
+    // codebook slot offset of this lane's rows within a stage (fixed slots)
+    const uint32_t pl_off0 = (uint32_t)(R::kIdxBytes + lane_slot * 32 + g * (kSlots * 32));
+
+    // One chunk: FULL when the chunk and the next one (or none) lie inside
+    // K, so that no activation load needs a column check.
+    auto chunk = [&](int c, uint32_t base, auto full_tag) {
+        constexpr bool FULL = decltype(full_tag)::value;
+        const uint32_t cu = (uint32_t)(c - c_begin);
         const uint4 w0 = lds128(base + g * 64 + 16 * t);
         const uint4 w1 = lds128(base + (g + 8) * 64 + 16 * t);
         LutPlanes P0, P1;
         if (GROUPED) {
-            const int s = p.G <= kChunk ? lane_slot : group_at(c * kChunk + 32 * t) - group_at(c * kChunk);
-            const uint32_t pb = base + R::kIdxBytes + s * 32;
-            planes_from_smem<T, PREPACKED>(pb + g * (NSLOT * 32), P0);
-            planes_from_smem<T, PREPACKED>(pb + (g + 8) * (NSLOT * 32), P1);
+            uint32_t pb;
+            if (cb_fixed) {
+                pb = base + pl_off0;
+            } else {
+                const int s = group_at(c * kChunk + 32 * t) - group_at(c * kChunk);
+                pb = base + R::kIdxBytes + s * 32 + g * (NSLOT * 32);
+            }
+            planes_from_smem<T, PREPACKED>(pb, P0);
+            planes_from_smem<T, PREPACKED>(pb + 8 * (kSlots * 32), P1);
         } else {
             P0 = PR0;
             P1 = PR1;
+        }
+        uint32_t xsc[NT] = {};
+        const uint16_t* xgc[NT] = {};
+        if constexpr (FULL) {
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt) {
+                if constexpr (XSMEM) xsc[tt] = mad_u32(cu, 2u * kChunk, xsa[tt]);
+                else xgc[tt] = static_cast<const uint16_t*>(ptr_mad(xga[tt], cu, 2u * kChunk));
+            }
         }
         const uint32_t ra[4] = {w0.x, w0.y, w0.z, w0.w};
         const uint32_t rb[4] = {w1.x, w1.y, w1.z, w1.w};
@@ -530,8 +618,17 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
             for (int tt = 0; tt < NT; ++tt) {
                 xv[tt] = xnext[tt];
                 // next pair: this chunk's ws+1, or the next chunk's first
-                const int kn = (c - c_begin) * kChunk + (ws < 3 ? 8 * (ws + 1) : kChunk);
-                if (ws < 3 || c + 1 < c_end) xnext[tt] = lds_x8(tt, kn);
+                if constexpr (FULL) {
+                    // byte offsets 16, 32, 48 in this chunk, then the next
+                    // chunk's first piece (ws is a constant once unrolled)
+                    if (ws == 0) xnext[tt] = x8_at<XSMEM, 16>(xsc[tt], xgc[tt]);
+                    else if (ws == 1) xnext[tt] = x8_at<XSMEM, 32>(xsc[tt], xgc[tt]);
+                    else if (ws == 2) xnext[tt] = x8_at<XSMEM, 48>(xsc[tt], xgc[tt]);
+                    else if (c + 1 < c_end) xnext[tt] = x8_at<XSMEM, 2 * kChunk>(xsc[tt], xgc[tt]);
+                } else {
+                    const int kn = (c - c_begin) * kChunk + (ws < 3 ? 8 * (ws + 1) : kChunk);
+                    if (ws < 3 || c + 1 < c_end) xnext[tt] = lds_x8(tt, kn);
+                }
             }
             const uint32_t sa = ra[ws] & 0x77777777u;
             const uint32_t ca = lop_and_or(mulhi(ra[ws], m31), 0x44444444u, 0x32103210u);
@@ -555,15 +652,18 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
                 }
             }
         }
-        if constexpr (RT > 0) {
+        if (RT > 0 && h_duty(c)) {
             // h += A[:, block] x[block]: lane (g, t) holds columns [8t, 8t+8)
             // of the block for A rows g, g+8 and token g (the k order inside
             // each MMA is the same permutation for both operands)
-            const int col = c * kChunk + 32 * warp + 8 * t;
+            const int col = c * kChunk + 32 * hblk + 8 * t;
             uint4 xa[NT];
 #pragma unroll
             for (int tt = 0; tt < NT; ++tt) {
-                if (!tok_ok[tt] || col >= p.K) {
+                if constexpr (FULL) {
+                    if constexpr (XSMEM) xa[tt] = lds128(mad_u32(cu, 2u * kChunk, xfa[tt]));
+                    else xa[tt] = ldg_keep_v4(ptr_mad(xgf[tt], cu, 2u * kChunk));
+                } else if (!tok_ok[tt] || col >= p.K) {
                     xa[tt] = make_uint4(0u, 0u, 0u, 0u);
                 } else if constexpr (XSMEM) {
                     xa[tt] = *reinterpret_cast<const uint4*>(xs + (8 * tt + g) * p.x_stride + (col - kb0));
@@ -585,6 +685,19 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
                 }
             }
         }
+    };
+
+    int st = 0;
+    for (int c = c_begin; c < c_end; ++c) {
+        cp_async_wait<S - 2>();  // this lane's copies of chunk c have landed
+        __syncwarp();            // ... and every lane's; the previous stage is free
+        issue(c + S - 1, st == 0 ? S - 1 : st - 1);
+        const uint32_t base = ring + (uint32_t)(st * R::kStageBytes);
+        st = st + 1 == S ? 0 : st + 1;
+        if ((XVEC || XSMEM) && (c + 1 < c_full || (c + 1 == c_end && c < c_full)))
+            chunk(c, base, BoolTag<true>{});
+        else
+            chunk(c, base, BoolTag<false>{});
     }
     if constexpr (RT > 0) {
         // the four warps' partial h [16 RT][MT] meet in their (now idle)
@@ -607,7 +720,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
         auto hsum = [&](int k, int tok) -> float {  // s * h[k][tok] over the CTA's K range
             float v = 0.f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) v += warp_part(w)[k * MT + tok];
+            for (int w = 0; w < WARPS; ++w) v += warp_part(w)[k * MT + tok];
             return p.scale * v;
         };
         auto pack = [](float lo, float hi) -> uint32_t {
@@ -661,6 +774,17 @@ __global__ void __launch_bounds__(kWarps * 32, 4) gemv_kernel(const GemvParams p
 
 constexpr int kStages = 3;  // measured: 3 >= 4 > 6 (more stages cost occupancy, not latency)
 
+// One CTA of 16 warps per SM: the whole SM's shared memory holds the
+// activations of the CTA's K range (up to 16 tokens x ~3.5K columns) beside
+// a 2-stage ring per warp, where 4 CTAs of 4 warps would have to read them
+// through L1.  Its 16 warps share one staged copy.
+constexpr int kBigWarps = 16;
+constexpr int kBigStages = 2;
+// shared memory one block may hold (static + dynamic) on sm_100
+constexpr size_t kMaxBlockSmem = 227 * 1024;
+// static shared memory of the kernel (the per-warp partial tiles)
+constexpr size_t gemv_static_smem(int nt, int warps) { return sizeof(float) * warps * kRowsPerTile * 8 * nt; }
+
 // codebook slots a 128-column chunk needs per row: 1 without grouping
 // (registers, no slot), 2 for groups of >= 128 columns, 4 for 32 and 64
 inline int codebook_slots(int G) { return G == 0 ? 0 : G >= kChunk ? 2 : 4; }
@@ -691,15 +815,16 @@ inline bool cluster_size_refused(cudaError_t e) {
 
 // Launches one variant; with `fit` set, reports instead how many of its
 // clusters the device holds at once (INT_MAX when it runs without clusters).
-template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int RT, int STAGES = kStages>
+template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int RT, int STAGES = kStages,
+          int WARPS = kWarps>
 int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, int* fit = nullptr) {
-    auto kern = gemv_kernel<T, NT, NSLOT, PREPACKED, XVEC, XSMEM, STAGES, RT>;
+    auto kern = gemv_kernel<T, NT, NSLOT, PREPACKED, XVEC, XSMEM, STAGES, RT, WARPS>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas, (unsigned)cs, 1);
-    cfg.blockDim = dim3(kWarps * 32, 1, 1);
-    const size_t smem = (size_t)p.x_bytes + (size_t)kWarps * STAGES * Ring<NSLOT, RT>::kStageBytes;
+    cfg.blockDim = dim3(WARPS * 32, 1, 1);
+    const size_t smem = (size_t)p.x_bytes + (size_t)WARPS * STAGES * Ring<NSLOT, RT>::kStageBytes;
     // the default limit covers static + dynamic shared memory up to 48 KB
-    constexpr size_t kStatic = sizeof(float) * kWarps * kRowsPerTile * 8 * NT;
+    constexpr size_t kStatic = gemv_static_smem(NT, WARPS);
     if (smem + kStatic > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return check_cuda(e, "gemv_kernel smem attribute");
@@ -745,7 +870,9 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, i
 // Defined in wlq_gemv_fold.cu.
 // stages2: a 2-stage ring, which lets the activations of 16 tokens be staged
 // beside the larger stages of this kernel.
-int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, bool stages2, int ctas, int cs,
+// big: one 16-warp CTA per SM with the activations staged (kBigWarps; r <= 32
+// and at most 16 tokens).
+int launch_fold(const GemvParams& p, int rt, bool bf16, bool xsmem, bool stages2, bool big, int ctas, int cs,
                 cudaStream_t stream, int* fit = nullptr);
 
 }  // namespace gemv

@@ -229,12 +229,15 @@ int launch_lora_h(const void* X, const void* A, float* H, int M, int K, int r, i
                      (reinterpret_cast<uintptr_t>(A) & 15) == 0;
     const int gx = (M + kHTok - 1) / kHTok;
     const int gz = (r + kHRank - 1) / kHRank;
-    // split K over a cluster (up to 16 CTAs) until about two CTAs per SM are
-    // in flight, keeping at least two k tiles per rank; no rank left empty
+    // split K over a cluster (up to 16 CTAs) while the grid still fits in one
+    // wave of four CTAs per SM (their shared-memory limit) -- the kernel is
+    // bound by the latency of its loads, so every resident CTA counts, and a
+    // second partial wave costs more than the split saves -- keeping at least
+    // two k tiles per rank; no rank left empty
     const int sms = device_sm_count();
     auto plan = [&](int cap) {
         int ks = 1;
-        while (ks < cap && (int64_t)gx * gz * ks < 2LL * sms && p.ktiles >= 2 * (ks + 1)) ++ks;
+        while (ks < cap && (int64_t)gx * gz * (ks + 1) <= 4LL * sms && p.ktiles >= 2 * (ks + 1)) ++ks;
         p.ktiles_per_rank = (p.ktiles + ks - 1) / ks;
         return (p.ktiles + p.ktiles_per_rank - 1) / p.ktiles_per_rank;
     };
