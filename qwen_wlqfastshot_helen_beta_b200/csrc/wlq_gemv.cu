@@ -299,11 +299,13 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     } else {
         int rc = search(false, pl);
         if (rc) return rc;
-        if (!pl.xsmem && big_ok) {
+        // measured: 16-warp CTAs also win where neither shape splits K
+        // (gate_up at M = 1: 43.4 -> 41.2 us), and lose where both split it
+        if (big_ok && (!pl.xsmem || pl.cs == 1)) {
             Plan b;
             rc = search(true, b);
             if (rc) return rc;
-            if (b.xsmem) pl = b;
+            if (b.xsmem && (!pl.xsmem || b.cs == 1)) pl = b;
         }
     }
     configure(pl.cs, pl.big);
