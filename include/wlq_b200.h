@@ -252,10 +252,14 @@ WLQ_API int wlq_gemv_allreduce(const int32_t* q_packed, const void* lut_c, const
  * the process split K over a cluster of exactly cs CTAs (1..16, at most one
  * per 128-column chunk; above 8 a non-portable cluster size the device must
  * accept), 0 restores the per-call choice.  wlq_gemv_last_split() returns the
- * split of the calling thread's last successful GEMV launch.  No reference
- * counterpart (the reference's split-K is internal, csrc/gemv_kernel.cu:422-428). */
+ * split of the calling thread's last successful GEMV launch and
+ * wlq_gemv_last_warps() its CTA shape: 4 (warps per CTA, 4 CTAs per SM) or 16
+ * (one CTA per SM, chosen where 4-warp CTAs could not keep the activations in
+ * shared memory, or where neither shape splits K).  No reference counterpart
+ * (the reference's split-K is internal, csrc/gemv_kernel.cu:422-428). */
 WLQ_API int wlq_gemv_set_split(int cs);
 WLQ_API int wlq_gemv_last_split(void);
+WLQ_API int wlq_gemv_last_warps(void);
 
 /* Device error word of `device`: bit 0 (WLQ_DEVERR_WAIT_TIMEOUT) is set when
  * a pipeline wait inside a tensor-core GEMM kernel gave up (the kernel then

@@ -129,6 +129,7 @@ namespace gemv {
 
 std::atomic<int> g_forced_split{0};
 thread_local int g_last_split = 0;
+thread_local int g_last_warps = 0;
 
 int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit) {
     static std::mutex mu;
@@ -321,7 +322,10 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     }
     if (rc == kRetryPortable)
         return fail(WLQ_ERR_CUDA, "wlq_gemv: the device refused a cluster of %d CTAs", pl.cs);
-    if (rc == WLQ_OK) g_last_split = pl.cs;
+    if (rc == WLQ_OK) {
+        g_last_split = pl.cs;
+        g_last_warps = pl.big ? kBigWarps : kWarps;
+    }
     return rc;
 }
 
@@ -337,5 +341,7 @@ int wlq_gemv_set_split(int cs) {
 }
 
 int wlq_gemv_last_split(void) { return wlq::gemv::g_last_split; }
+
+int wlq_gemv_last_warps(void) { return wlq::gemv::g_last_warps; }
 
 }  // extern "C"

@@ -798,9 +798,11 @@ inline int ring_stage_bytes(int slots, int rt) { return kRowsPerTile * 64 + kRow
 int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit);
 
 // Split forced by wlq_gemv_set_split (0 = chosen per call) and the split of
-// this thread's last launch (wlq_gemv_last_split).
+// this thread's last launch (wlq_gemv_last_split) and its warps per CTA
+// (wlq_gemv_last_warps).
 extern std::atomic<int> g_forced_split;
 extern thread_local int g_last_split;
+extern thread_local int g_last_warps;
 
 // Returned by a launch whose non-portable cluster size (> 8) the device
 // refused (the error is cleared): the caller retries at 8 CTAs or fewer.

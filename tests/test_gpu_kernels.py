@@ -187,6 +187,44 @@ def test_gemv_forced_split_matches_oracle(split):
         _lib.check(lib.wlq_gemv_set_split(17), "wlq_gemv_set_split")
 
 
+@pytest.mark.parametrize("G,goff", [(0, 0), (64, 0), (128, 64)], ids=["per_row", "g64", "g128_off64"])
+@pytest.mark.parametrize("r", [0, 16, 32], ids=["h_given", "h_r16", "h_r32"])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_gemv_16warp_ctas_match_oracle(G, goff, r, dtype):
+    """The one-CTA-per-SM shape (16 warps sharing one staged copy of the
+    activations, a 2-stage ring per warp) against the oracle: K unsplit
+    (forced split 1) with a ragged last 128-column chunk, 8 and 16 tokens
+    (activations too large for 4-warp CTAs to stage), per-row and per-group
+    codebooks, h given (r = 0 here) and h computed in the kernel (rank 16 and
+    32), and wlq_gemv_last_warps reporting the shape that ran."""
+    from qwen_wlqfastshot_helen_beta_b200 import _lib
+    lib = _lib.lib
+    rng = np.random.default_rng(100 + G + r + goff)
+    N = 80
+    _lib.check(lib.wlq_gemv_set_split(1), "wlq_gemv_set_split")
+    try:
+        for M, K in ((8, 3104), (16, 1440)):
+            L = make_np_layer(rng, N, K, G, goff, density=0.01, r=max(r, 16))
+            T = dev_layer(L)
+            x, h = inputs(rng, L, M, dtype)
+            ref = reference_output(L, x.float().cpu().numpy(), h.cpu().numpy())
+            if r == 0:
+                y = run_ours(L, T, x, h, gemv=True, fmt=1)
+            else:
+                lut = C().prepack_lut(T["lut"], dtype)
+                cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], N, K, 4, dtype, G,
+                                                  goff)
+                y = torch.full((M, N), float("nan"), dtype=dtype, device="cuda")
+                C().gemv_lora_a(T["q"], lut, x, y, N, K, 4, T["off"], cols, vals, T["B"], T["A"].to(dtype).contiguous(),
+                                T["gamma"], L.scale, G, goff)
+                torch.cuda.synchronize()
+            assert lib.wlq_gemv_last_warps() == 16, (M, K)
+            assert lib.wlq_gemv_last_split() == 1
+            assert rel_err(y.float().cpu().numpy(), ref) <= TOL[dtype], (M, K)
+    finally:
+        _lib.check(lib.wlq_gemv_set_split(0), "wlq_gemv_set_split")
+
+
 @pytest.mark.parametrize("M,K,r", [(1, 3584, 16), (7, 1000, 48), (64, 3584, 64), (200, 4864, 48), (512, 18944, 16),
                                    (2048, 3584, 80), (8192, 3584, 48), (33, 1004, 16), (130, 3586, 24)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
