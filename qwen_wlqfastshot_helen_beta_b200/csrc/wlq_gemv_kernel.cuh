@@ -222,6 +222,9 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_kernel(const Gemv
     __shared__ float part[WARPS][kRowsPerTile][MT];   // per-warp partial tile
 
     const int warp = threadIdx.x >> 5;
+    // the next launch in the stream (a programmatic dependent launch) may
+    // begin its weight prologue on the SMs this grid's CTAs leave
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2;
     const int t = lane & 3;
@@ -359,10 +362,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_kernel(const Gemv
     };
 #pragma unroll
     for (int j = 0; j < S - 1; ++j) issue(c_begin + j, j);
-    // this rank's activations into shared memory (XSMEM), waited for after
-    // the low-rank MMA; larger slices are read through L1
     const int kb0 = c_begin * kChunk;
-    if (XSMEM) stage_x_issue<T, XVEC>(xs, x, p.M, p.K, kb0, p.chunks_per_rank * kChunk, p.x_stride);
 
     // per-row codebooks (no grouping) stay in registers for the whole K range
     LutPlanes PR0, PR1;
@@ -416,6 +416,14 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_kernel(const Gemv
                 for (int i = 0; i < 4; ++i) hacc[rt][tt][i] = 0.f;
         }
     }
+    // Everything above reads weights only.  The activations, h and the
+    // output follow the previous kernel in stream order: launched as a
+    // programmatic dependent launch, this grid starts while the previous one
+    // drains and waits here for it to complete (a no-op otherwise).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // this rank's activations into shared memory (XSMEM), waited for after
+    // the low-rank MMA; larger slices are read through L1
+    if (XSMEM) stage_x_issue<T, XVEC>(xs, x, p.M, p.K, kb0, p.chunks_per_rank * kChunk, p.x_stride);
     if (RT == 0 && p.r > 0 && (gridDim.y == 1 || cluster_ctarank() == 0u)) {
         for (int kb = 0; kb < p.r; kb += 16) {
             uint32_t a[4];
@@ -845,7 +853,7 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, i
     }
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];  // clusters split K: cs CTAs along y
+    cudaLaunchAttribute attr[2];  // clusters split K: cs CTAs along y
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = (unsigned)cs;
@@ -858,6 +866,16 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, i
             return WLQ_OK;
         }
         return clusters_that_fit(reinterpret_cast<const void*>(kern), cfg, fit);
+    }
+    // Programmatic dependent launch (measured: 439.0 -> 424.2 us over the 16
+    // decode configurations, every one faster).  The grid launches once every
+    // CTA of the previous grid has started (each triggers on entry), so its
+    // CTAs only take SM room that grid no longer needs.  Not for the fused
+    // all-reduce, whose calls must not overlap.
+    if (p.tp_world <= 1) {
+        attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+        ++cfg.numAttrs;
     }
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess && cs > 8 && cluster_size_refused(e)) {
