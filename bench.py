@@ -190,6 +190,8 @@ def bench_config(world, copies=3):
         "parallelism": f"tp{world}" if world > 1 else "single",
         "l2": f"inputs larger than L2: {copies} rotating weight copies per rank",
         "timing": "CUDA graph of K steps without per-launch nodes, events around the replay",
+        "launch": "consecutive GEMV launches overlap (wlq_gemv_set_overlap(1), programmatic dependent launch): "
+                  "weights are static during the timed steps",
     }
 
 
@@ -237,6 +239,12 @@ def run_ours(args):
                 calls.append((c, name, M, L, x, L.lora_A_act, out))
     lib = _lib.lib
     stream = torch.cuda.current_stream()
+    # the weights are written (built, prepacked) before this point and never
+    # during the timed steps: consecutive GEMV launches may overlap
+    # (wlq_gemv_set_overlap: a GEMV reads its weights before the previous
+    # kernel in the stream has completed)
+    torch.cuda.synchronize()
+    _lib.check(lib.wlq_gemv_set_overlap(1), "wlq_gemv_set_overlap")
 
     # row-parallel layers (o, down) at N > 1: the all-reduce fused into the
     # GEMV over NVLink peer memory (wlq_gemv_allreduce)
@@ -699,6 +707,7 @@ def cpu_baseline_config0(dev, budget_s=15.0, reps=50):
     A = torch.from_numpy(L.lora_A).to(d)
     B = torch.from_numpy(L.lora_B).to(d)
     gam = torch.from_numpy(L.dora_gamma).to(d)
+    torch.cuda.synchronize()  # weights complete before any (overlapping) GEMV reads them
     rng = np.random.default_rng(4)
     x_np = rng.standard_normal((M0, K0)).astype(np.float32)
     x_host = torch.from_numpy(x_np).pin_memory()

@@ -261,6 +261,22 @@ WLQ_API int wlq_gemv_set_split(int cs);
 WLQ_API int wlq_gemv_last_split(void);
 WLQ_API int wlq_gemv_last_warps(void);
 
+/* Opt-in overlap of consecutive decode GEMV launches in a stream (process
+ * wide; off by default).  With wlq_gemv_set_overlap(1), every later
+ * wlq_gemv / wlq_gemv_lora_a / wlq_gemm-as-GEMV launch (not the fused
+ * all-reduce) is a programmatic dependent launch: it may start while the
+ * kernel before it in the stream is still running and read its WEIGHTS
+ * (q_packed, codebooks, outlier records and offsets, lora_A / lora_B, gamma)
+ * before that kernel's writes are visible; activations, h and out are only
+ * touched after the previous kernel has completed.  Enable it only where no
+ * kernel launched immediately before a GEMV call in the same stream writes
+ * that layer's weights -- true for inference once the weights are loaded and
+ * the device synchronised -- and keep it off while weights are being written
+ * (loading, prepacking).  wlq_gemv_get_overlap() returns the setting.  No
+ * reference counterpart (the reference launches its kernels plainly). */
+WLQ_API int wlq_gemv_set_overlap(int on);
+WLQ_API int wlq_gemv_get_overlap(void);
+
 /* Device error word of `device`: bit 0 (WLQ_DEVERR_WAIT_TIMEOUT) is set when
  * a pipeline wait inside a tensor-core GEMM kernel gave up (the kernel then
  * abandons its tile and its output is undefined).  Synchronous; clears the

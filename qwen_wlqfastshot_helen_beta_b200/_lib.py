@@ -47,6 +47,8 @@ SIGNATURES = {
     "wlq_gemv_set_split": (_i32, [_i32]),
     "wlq_gemv_last_split": (_i32, []),
     "wlq_gemv_last_warps": (_i32, []),
+    "wlq_gemv_set_overlap": (_i32, [_i32]),
+    "wlq_gemv_get_overlap": (_i32, []),
     "wlq_tp_buffer_bytes": (ctypes.c_size_t, [_i32, _i32]),
     "wlq_tp_buffer_alloc": (_i32, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
     "wlq_tp_buffer_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),

@@ -128,6 +128,7 @@ struct FitKey {
 namespace gemv {
 
 std::atomic<int> g_forced_split{0};
+std::atomic<int> g_overlap{0};
 thread_local int g_last_split = 0;
 thread_local int g_last_warps = 0;
 
@@ -343,5 +344,13 @@ int wlq_gemv_set_split(int cs) {
 int wlq_gemv_last_split(void) { return wlq::gemv::g_last_split; }
 
 int wlq_gemv_last_warps(void) { return wlq::gemv::g_last_warps; }
+
+int wlq_gemv_set_overlap(int on) {
+    if (on != 0 && on != 1) return wlq::fail(WLQ_ERR_INVALID_ARG, "wlq_gemv_set_overlap: expected 0 or 1, got %d", on);
+    wlq::gemv::g_overlap.store(on, std::memory_order_relaxed);
+    return WLQ_OK;
+}
+
+int wlq_gemv_get_overlap(void) { return wlq::gemv::g_overlap.load(std::memory_order_relaxed); }
 
 }  // extern "C"

@@ -809,6 +809,9 @@ int clusters_that_fit(const void* kern, const cudaLaunchConfig_t& cfg, int* fit)
 // this thread's last launch (wlq_gemv_last_split) and its warps per CTA
 // (wlq_gemv_last_warps).
 extern std::atomic<int> g_forced_split;
+// Programmatic dependent launch of the GEMV (wlq_gemv_set_overlap), off by
+// default.
+extern std::atomic<int> g_overlap;
 extern thread_local int g_last_split;
 extern thread_local int g_last_warps;
 
@@ -867,12 +870,15 @@ int launch_variant(const GemvParams& p, int ctas, int cs, cudaStream_t stream, i
         }
         return clusters_that_fit(reinterpret_cast<const void*>(kern), cfg, fit);
     }
-    // Programmatic dependent launch (measured: 439.0 -> 424.2 us over the 16
-    // decode configurations, every one faster).  The grid launches once every
+    // Programmatic dependent launch, when the caller opted in
+    // (wlq_gemv_set_overlap; measured: 439.0 -> 413.6 us over the 16 decode
+    // configurations, every one faster).  The grid may start as soon as every
     // CTA of the previous grid has started (each triggers on entry), so its
-    // CTAs only take SM room that grid no longer needs.  Not for the fused
-    // all-reduce, whose calls must not overlap.
-    if (p.tp_world <= 1) {
+    // CTAs only take SM room that grid no longer needs; its weight prologue
+    // then runs before the previous kernel's writes are visible, which is why
+    // the caller must guarantee that kernel wrote none of this layer's
+    // weights.  Not for the fused all-reduce, whose calls must not overlap.
+    if (p.tp_world <= 1 && g_overlap.load(std::memory_order_relaxed) != 0) {
         attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
         ++cfg.numAttrs;

@@ -494,3 +494,62 @@ def test_prepack_outlier_records():
                 assert np.array_equal(rec[a:b] >> 16, vbits), r
                 cb = torch.from_numpy(Wcb[r, gcol]).to(dtype).float().numpy()
                 assert np.array_equal(delta[a:b], ov.float().numpy() - cb), r
+
+
+def test_gemv_overlap_opt_in_matches_plain_launches():
+    """wlq_gemv_set_overlap: off by default; with it on, consecutive GEMV
+    launches (programmatic dependent launches, weights read before the
+    previous kernel completes) give bit-identical outputs to plain launches,
+    for a chain where each call's input is the previous call's output, with
+    4-warp CTAs (1 and 2 tokens) and 16-warp CTAs (9 and 16 tokens on an
+    unsplit K of 1440, a ragged last chunk).  The weights are written and the device
+    synchronised before the overlapping calls, as the contract asks."""
+    from qwen_wlqfastshot_helen_beta_b200 import _lib
+    lib = _lib.lib
+    assert lib.wlq_gemv_get_overlap() == 0
+    dtype = torch.bfloat16
+    rng = np.random.default_rng(77)
+    K = 1440
+    layers = []
+    for N in (K, K, 80):
+        L = make_np_layer(rng, N, K, 128, 0, density=0.01, r=16)
+        T = dev_layer(L)
+        lut = C().prepack_lut(T["lut"], dtype)
+        cols, vals = C().prepack_outliers(T["q"], T["lut"], T["off"], T["cols"], T["vals"], N, K, 4, dtype, 128, 0)
+        layers.append((L, T, lut, cols, vals, T["A"].to(dtype).contiguous()))
+    torch.cuda.synchronize()
+
+    def chain(M):
+        x = torch.from_numpy(np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)).to("cuda", dtype)
+        outs, warps = [], []
+        for L, T, lut, cols, vals, A in layers:
+            y = torch.empty((M, L.N), dtype=dtype, device="cuda")
+            C().gemv_lora_a(T["q"], lut, x, y, L.N, L.K, 4, T["off"], cols, vals, T["B"], A, T["gamma"], L.scale, 128, 0)
+            warps.append(lib.wlq_gemv_last_warps())
+            outs.append(y)
+            if L.N == K:
+                x = y  # the next call reads this call's output
+        torch.cuda.synchronize()
+        return [o.cpu() for o in outs], warps
+
+    _lib.check(lib.wlq_gemv_set_split(1), "wlq_gemv_set_split")
+    try:
+        shapes = set()
+        for M in (1, 2, 9, 16):
+            plain, wp = chain(M)
+            _lib.check(lib.wlq_gemv_set_overlap(1), "wlq_gemv_set_overlap")
+            try:
+                assert lib.wlq_gemv_get_overlap() == 1
+                over, wo = chain(M)
+            finally:
+                _lib.check(lib.wlq_gemv_set_overlap(0), "wlq_gemv_set_overlap")
+            assert wp == wo, (M, wp, wo)
+            shapes.update(wp)
+            for a, b in zip(plain, over):
+                assert torch.isfinite(a.float()).all()
+                assert torch.equal(a, b), M
+        assert shapes == {4, 16}, shapes
+    finally:
+        _lib.check(lib.wlq_gemv_set_split(0), "wlq_gemv_set_split")
+    with pytest.raises(RuntimeError, match="0 or 1"):
+        _lib.check(lib.wlq_gemv_set_overlap(2), "wlq_gemv_set_overlap")
