@@ -191,6 +191,7 @@ int launch_gemv(const LinearArgs& a, cudaStream_t stream) {
     p.tp_nmax = a.tp_nmax;
     if (a.tp_world > 1) {
         const TpLayout l = tp_layout(a.tp_world, a.tp_nmax);
+        p.tp_stride = l.stride;
         for (int q = 0; q < a.tp_world; ++q) {
             char* b = static_cast<char*>(a.tp_bufs[q]);
             p.tp_data[q] = reinterpret_cast<unsigned long long*>(b + l.data);

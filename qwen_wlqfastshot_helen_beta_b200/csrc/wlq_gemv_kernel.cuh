@@ -42,8 +42,9 @@ struct GemvParams {
     uint32_t mul16, mul31; // 1<<16 and 1<<31, runtime values so mul.hi stays a multiply
     // fused tensor-parallel all-reduce (row-parallel layers), tp_world > 1
     int tp_world, tp_rank, tp_nmax;
-    unsigned long long* tp_data[kMaxTp];  // each rank's slots [2 parities][world][16 tokens][tp_nmax]:
-                                          // fp32 value bits | epoch << 32
+    int tp_stride;                        // words per (parity, rank, token) row of each rank's slots
+    unsigned long long* tp_data[kMaxTp];  // each rank's slots [2 parities][world][16 tokens][tp_stride]:
+                                          // per tile eight words of two 16-bit values | epoch << 32
     uint32_t* tp_counters;       // this rank's per-tile call counters [tiles]
     uint32_t* tp_err;            // this rank's error word
 };
@@ -126,76 +127,107 @@ struct Ring {
     static constexpr int kStageBytes = kIdxBytes + kPlaneBytes + kABytes;
 };
 
-// 8-byte slot accesses that reach the other GPUs' memory and are never
-// cached or merged: one store carries a value and its epoch together.
-__device__ __forceinline__ void st_slot(unsigned long long* a, unsigned long long v) {
-    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+// 16-byte slot accesses that reach the other GPUs' memory and are never
+// cached or merged.  Each 8-byte half is written and read whole (single-copy
+// atomic) and carries its own epoch, so a reader that sees one half of a
+// pair early simply reads the pair again.
+__device__ __forceinline__ void st_slot2(unsigned long long* a, unsigned long long v0, unsigned long long v1) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(a), "l"(v0), "l"(v1) : "memory");
 }
-__device__ __forceinline__ unsigned long long ld_slot(const unsigned long long* a) {
-    unsigned long long v;
-    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
-    return v;
+__device__ __forceinline__ void ld_slot2(const unsigned long long* a, unsigned long long& v0, unsigned long long& v1) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "l"(a) : "memory");
 }
 
 // Row-parallel epilogue with the all-reduce fused, for one warp's 16-row
-// tile (cluster rank 0).  Each of the tile's gamma-scaled partial values goes
-// to every other rank as ONE 8-byte store holding the value and the call's
-// epoch, so a reader knows a slot is complete once its epoch matches: no
-// fences and no separate flags on the way (a system-scope fence per tile cost
-// ~25 us per call over NVLink).  Epochs come from a per-tile call counter that
-// advances identically on every rank, so CUDA graph replays need no host
-// input; slots alternate by epoch parity, and a rank cannot run two calls
-// ahead on a tile because each call waits for all ranks' values of the
-// previous one.  Every rank adds the ranks' values in rank order, so all ranks
-// hold the same result bit for bit.  The waits share one 2 s deadline; when
-// it passes the error word is set and the output is undefined.
+// tile (cluster rank 0).  First every lane finishes its elements of the tile
+// (the K-split sum over the cluster, times the row's DoRA magnitude) in place
+// in the warp's own partial tile, rounded to the activation type -- what a
+// rank's output would carry into an all-reduce after the GEMV.  Then the
+// values go out packed two to an 8-byte word with the call's 32-bit epoch;
+// two words (rows 4pg .. 4pg + 3 of one token) go to every other rank in one
+// 16-byte store.  A reader knows a word is complete once its epoch matches:
+// no fences and no separate flags on the way (a system-scope fence per tile
+// cost ~25 us per call over NVLink), and four values per store instead of
+// one.  Epochs come from a per-tile call counter that advances identically
+// on every rank, so CUDA graph replays need no host input; slots alternate by
+// epoch parity, and a rank cannot run two calls ahead on a tile because each
+// call waits for all ranks' values of the previous one.  Every rank adds the
+// same rounded values in rank order, so all ranks hold the same result bit
+// for bit.  The waits share one 2 s deadline; when it passes the error word
+// is set and the output is undefined.
 template <typename T, int MT>
 __device__ void tp_allreduce_tile(const GemvParams& p, float (*part)[MT], uint32_t nranks, int tile_row0, int lane,
                                   float gam) {
-    constexpr int kPer = (kRowsPerTile * MT + 31) / 32;  // tile elements per lane
+    // lane owns elements e = lane + 32 i: row e % 16 (= lane % 16, whose
+    // magnitude `gam` is), token e / 16.  Only this warp reads or writes its
+    // own tile here; the other cluster ranks' tiles are only read.
+#pragma unroll
+    for (int e = lane; e < kRowsPerTile * MT; e += 32) {
+        const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
+        const int n = tile_row0 + rl;
+        float v = 0.f;
+        if (n < p.N && tk < p.M) v = cluster_sum(&part[rl][tk], nranks) * gam;
+        part[rl][tk] = ActTraits<T>::to_f32(ActTraits<T>::from_f32(v));
+    }
+    __syncwarp();
+    // pair pr = (token tk, group pg): words 2pg and 2pg + 1 of the token's
+    // eight, word w holding rows 2w and 2w + 1 of the tile
+    constexpr int kPairs = 4 * MT;
+    constexpr int kPer = (kPairs + 31) / 32;
     const int tile = tile_row0 / kRowsPerTile;
     const int world = p.tp_world, me = p.tp_rank;
     uint32_t cnt = lane == 0 ? p.tp_counters[tile] + 1u : 0u;
     cnt = __shfl_sync(0xFFFFFFFFu, cnt, 0);
     const int par = (int)(cnt & 1u);
     const unsigned long long tag = (unsigned long long)cnt << 32;
-    float own[kPer];
+    auto slot_of = [&](int src, int tk, int pg) {
+        return ((int64_t)(par * world + src) * kRowsPerTile + tk) * p.tp_stride + tile * 8 + 2 * pg;
+    };
+    auto bits = [](float v) {  // v is exactly representable in T
+        const T t = ActTraits<T>::from_f32(v);
+        return (unsigned long long)*reinterpret_cast<const uint16_t*>(&t);
+    };
+    unsigned long long mine[kPer][2];
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
-        const int e = lane + 32 * i;
-        const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
-        const int n = tile_row0 + rl;
-        own[i] = 0.f;
-        if (e >= kRowsPerTile * MT || n >= p.N || tk >= p.M) continue;
-        own[i] = cluster_sum(&part[rl][tk], nranks) * gam;
-        const int64_t slot = ((int64_t)(par * world + me) * kRowsPerTile + tk) * p.tp_nmax + n;
+        const int pr = lane + 32 * i;
+        const int tk = pr >> 2, pg = pr & 3;
+        mine[i][0] = mine[i][1] = 0ull;
+        if (pr >= kPairs || tk >= p.M) continue;
+        mine[i][0] = tag | bits(part[4 * pg][tk]) | (bits(part[4 * pg + 1][tk]) << 16);
+        mine[i][1] = tag | bits(part[4 * pg + 2][tk]) | (bits(part[4 * pg + 3][tk]) << 16);
+        const int64_t slot = slot_of(me, tk, pg);
         for (int q = 0; q < world; ++q)
-            if (q != me) st_slot(p.tp_data[q] + slot, tag | __float_as_uint(own[i]));
+            if (q != me) st_slot2(p.tp_data[q] + slot, mine[i][0], mine[i][1]);
     }
     const uint64_t deadline = globaltimer_ns() + 2000000000ull;
     bool ok = true;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
-        const int e = lane + 32 * i;
-        const int rl = e % kRowsPerTile, tk = e / kRowsPerTile;
-        const int n = tile_row0 + rl;
-        if (e >= kRowsPerTile * MT || n >= p.N || tk >= p.M) continue;
-        float s = 0.f;
+        const int pr = lane + 32 * i;
+        const int tk = pr >> 2, pg = pr & 3;
+        if (pr >= kPairs || tk >= p.M) continue;
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
         for (int q = 0; q < world; ++q) {
-            if (q == me) {
-                s += own[i];
-                continue;
+            unsigned long long w0 = mine[i][0], w1 = mine[i][1];
+            if (q != me) {
+                const unsigned long long* a = p.tp_data[me] + slot_of(q, tk, pg);
+                ld_slot2(a, w0, w1);
+                while (((uint32_t)(w0 >> 32) != cnt || (uint32_t)(w1 >> 32) != cnt) && ok) {
+                    if (globaltimer_ns() > deadline) ok = false;  // a rank never arrived: give up
+                    else ld_slot2(a, w0, w1);
+                }
             }
-            const unsigned long long* a =
-                p.tp_data[me] + ((int64_t)(par * world + q) * kRowsPerTile + tk) * p.tp_nmax + n;
-            unsigned long long w = ld_slot(a);
-            while ((uint32_t)(w >> 32) != cnt && ok) {
-                if (globaltimer_ns() > deadline) ok = false;  // a rank never arrived: give up
-                else w = ld_slot(a);
-            }
-            s += __uint_as_float((uint32_t)w);
+            s[0] += ActTraits<T>::bits_to_f32((uint16_t)w0);
+            s[1] += ActTraits<T>::bits_to_f32((uint16_t)(w0 >> 16));
+            s[2] += ActTraits<T>::bits_to_f32((uint16_t)w1);
+            s[3] += ActTraits<T>::bits_to_f32((uint16_t)(w1 >> 16));
         }
-        reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = tile_row0 + 4 * pg + j;
+            if (n < p.N) reinterpret_cast<T*>(p.out)[(int64_t)tk * p.N + n] = ActTraits<T>::from_f32(s[j]);
+        }
     }
     if (!ok) atomicOr(p.tp_err, 1u);
     __syncwarp();

@@ -53,15 +53,21 @@ struct LinearArgs {
 // call that wrote it.
 struct TpLayout {
     size_t err, counters, data, total;
+    int stride;  // 8-byte words per (parity, source rank, token) row of the data region
 };
 constexpr size_t tp_round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+// The data region holds, per parity, source rank and token, eight 8-byte words
+// per 16-row tile (two 16-bit values and a 32-bit epoch each), written in
+// 16-byte pairs: the stride is even and holds every tile's eight words.
 constexpr TpLayout tp_layout(int world, int max_N) {
     const size_t tiles = (size_t)(max_N + 15) / 16;
     TpLayout l{};
     l.err = 0;
     l.counters = 128;
     l.data = tp_round_up(l.counters + 4 * tiles, 256);
-    l.total = tp_round_up(l.data + 2ull * world * 16 * (size_t)max_N * 8, 256);
+    const size_t words = 8 * tiles > (size_t)max_N ? 8 * tiles : (size_t)max_N;
+    l.stride = (int)tp_round_up(words, 2);
+    l.total = tp_round_up(l.data + 2ull * world * 16 * (size_t)l.stride * 8, 256);
     return l;
 }
 
