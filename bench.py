@@ -426,28 +426,21 @@ def run_ours(args):
         e2e_enqueue()
         torch.cuda.current_stream().synchronize()
 
-    # the graphed step pipelines the same copies: every call's activations
-    # go over on one copy stream ahead of its launch and its output comes
-    # back on another as soon as it is written, all inside the step (the 16
-    # calls of a step are independent; the host still waits for the whole
-    # step's outputs)
-    s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    in_slices = [(view(in_dev, o, t), view(in_host, o, t)) for t, o in zip(ins, in_offs)]
+    # the graphed step overlaps the read-back: the step's activations go over
+    # in one copy, and every call's output comes back on a copy stream as
+    # soon as it is written, while the step's later calls run (the 16 calls
+    # of a step are independent; the host still waits for the whole step's
+    # outputs).  Per-call input copies were measured too: their events add a
+    # plain dependency to every launch, which cost the GEMV launch overlap
+    # (-8 % at 2 GPUs).
+    s_d2h = torch.cuda.Stream()
     out_slices = [(view(out_host, o, t), view(out_dev, o, t)) for t, o in zip(outs, out_offs)]
 
     def e2e_enqueue_pipelined():
         main = torch.cuda.current_stream()
-        s_h2d.wait_stream(main)
         s_d2h.wait_stream(main)
-        ready = []
-        with torch.cuda.stream(s_h2d):
-            for dst, src in in_slices:
-                dst.copy_(src, non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(s_h2d)
-                ready.append(ev)
+        in_dev.copy_(in_host, non_blocking=True)
         for i, (name, L, xd, a, od) in enumerate(host):
-            main.wait_event(ready[i])
             if comm is not None and name in ("o", "down"):
                 _C.gemv_allreduce(comm, xd, L.q_packed, L.lut_packed, od, L.N, L.K, 4, L.words_per_row,
                                   L.chunk_offsets, L.cols_packed, L.delta_packed, None, L.lora_B, L.dora_gamma,
@@ -462,7 +455,6 @@ def run_ours(args):
             s_d2h.wait_event(done)
             with torch.cuda.stream(s_d2h):
                 out_slices[i][0].copy_(out_slices[i][1], non_blocking=True)
-        main.wait_stream(s_h2d)
         main.wait_stream(s_d2h)
 
     def timed_e2e(step_fn):
@@ -489,10 +481,11 @@ def run_ours(args):
     g_e2e = torch.cuda.CUDAGraph()
     s_e2e = torch.cuda.Stream()
     s_e2e.wait_stream(torch.cuda.current_stream())
+    enqueue = e2e_enqueue_pipelined if args.e2e_copies == "pipelined" else e2e_enqueue
     with torch.cuda.stream(s_e2e):
-        e2e_enqueue_pipelined()
+        enqueue()
         with torch.cuda.graph(g_e2e, stream=s_e2e):
-            e2e_enqueue_pipelined()
+            enqueue()
     torch.cuda.current_stream().wait_stream(s_e2e)
     torch.cuda.synchronize()
 
@@ -554,11 +547,11 @@ def run_ours(args):
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "path": "torch.ops.wlq_fastShot.gemm(..., lora_A) on every (linear, M) of a step (h = A x "
-"inside the GEMV); every call's activations copied from pinned host memory and its output read "
-                            "back into pinned host memory, every step, on two copy streams: each copy overlaps the "
-                            "other calls of the step, none crosses a step boundary; the step replayed as one CUDA "
-                            "graph (as vLLM runs decode), host synchronised per step; eager_value: one copy in, "
-                            "the calls, one copy out, no overlap",
+"inside the GEMV); every step the step's activations copied in from one pinned host buffer, "
+                            "and every call's output read back into pinned host memory on a copy stream as soon as it "
+                            "is written (overlapping the step's later calls; no copy crosses a step boundary); the "
+                            "step replayed as one CUDA graph (as vLLM runs decode), host synchronised per step; "
+                            "eager_value: one copy in, the calls, one copy out, no overlap",
                     "eager_value": round(eager_value, 1)},
             "gpu_launches": 16 * args.steps,
             "clocks": clk.summary(),
@@ -1175,6 +1168,9 @@ def run_vllm_decode(args):
 
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--e2e-copies", choices=("pipelined", "single"), default="pipelined",
+                    help="e2e graph: one copy in, then every call's output read back on a copy stream while the "
+                         "step's later calls run (default), or one copy in and one out around the calls")
     ap.add_argument("--case", default=None, help="name:M (M <= 16: GEMV; larger: GEMM), one configuration for "
                     "profiling; a gemm: prefix is accepted")
     ap.add_argument("--gpus", type=int, default=1)
