@@ -102,7 +102,8 @@ int dispatch_big(const GemvParams& p, int ctas, int cs, cudaStream_t stream, int
 template <typename T>
 int dispatch(const GemvParams& p, bool prepacked, bool xvec, bool xsmem, bool big, int ctas, int cs,
              cudaStream_t stream, int* fit) {
-    if (big) return p.M <= 8 ? dispatch_big<T, 1>(p, ctas, cs, stream, fit) : dispatch_big<T, 2>(p, ctas, cs, stream, fit);
+    if (big)
+        return p.M <= 8 ? dispatch_big<T, 1>(p, ctas, cs, stream, fit) : dispatch_big<T, 2>(p, ctas, cs, stream, fit);
     if (p.M > 16) return dispatch32<T>(p, xsmem, ctas, cs, stream, fit);
     return p.M <= 8 ? dispatch_slots<T, 1>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit)
                     : dispatch_slots<T, 2>(p, prepacked, xvec, xsmem, ctas, cs, stream, fit);

@@ -16,9 +16,11 @@ namespace {
 template <typename T, int NT, int NSLOT>
 int fold_x(const GemvParams& p, int rt, bool xsmem, bool stages2, bool big, int ctas, int cs, cudaStream_t stream,
            int* fit) {
-    if (big)  // one 16-warp CTA per SM, activations staged (r <= 32)
-        return rt == 1 ? launch_variant<T, NT, NSLOT, true, true, true, 1, kBigStages, kBigWarps>(p, ctas, cs, stream, fit)
-                       : launch_variant<T, NT, NSLOT, true, true, true, 2, kBigStages, kBigWarps>(p, ctas, cs, stream, fit);
+    if (big) {  // one 16-warp CTA per SM, activations staged (r <= 32)
+        if (rt == 1) return launch_variant<T, NT, NSLOT, true, true, true, 1, kBigStages, kBigWarps>(p, ctas, cs,
+                                                                                                      stream, fit);
+        return launch_variant<T, NT, NSLOT, true, true, true, 2, kBigStages, kBigWarps>(p, ctas, cs, stream, fit);
+    }
     if (rt == 3)  // r <= 48 (a fused qkv of three rank-16 adapters): always a 2-stage ring
         return xsmem ? launch_variant<T, NT, NSLOT, true, true, true, 3, 2>(p, ctas, cs, stream, fit)
                      : launch_variant<T, NT, NSLOT, true, true, false, 3, 2>(p, ctas, cs, stream, fit);
