@@ -95,23 +95,34 @@ def test_gemm_rank_above_one_step():
     assert rel_err(y.float().cpu().numpy(), ref) <= TOL[torch.float16]
 
 
+def _oracle_rows(L, N, K, rows):
+    """Oracle (bit-exact) dequantised weights of the sampled rows, their B
+    rows and magnitudes, and A in float64."""
+    W = O.dequant(L.q_packed.cpu().numpy(), L.words_per_row, L.lut_c.cpu().numpy(), N, K, 4, 128, 0,
+                  L.chunk_offsets.cpu().numpy(), L.chunk_cols.cpu().numpy(), L.chunk_vals.cpu().numpy())
+    return (np.ascontiguousarray(W[rows]), L.lora_B.cpu().numpy()[rows], L.dora_gamma.cpu().numpy()[rows],
+            L.lora_A.float().cpu().numpy().astype(np.float64))
+
+
 @pytest.mark.parametrize("name,M", [("qkv", 512), ("o", 2048), ("down", 512)])
 def test_gemm_full_size_shapes(name, M):
     """BASELINE config-2 shapes with the benchmark recipe against the
-    dequantised weights times x in fp32 on the GPU."""
+    oracle's float64 forward on 128 sampled rows x 64 sampled tokens over the
+    full K (h given, and h from wlq_lora_h as the prefill op runs it)."""
     from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
     K, N = S.QWEN25_7B[name]
     L = S.make_layer(N, K, group_size=128, density=0.005, r=16, seed=12)
-    W = torch.empty((N, K), dtype=torch.float16, device="cuda")
-    C().dequant_w0(L.q_packed, L.lut_c, W, N, K, 4, L.words_per_row, L.chunk_offsets, L.chunk_cols, L.chunk_vals,
-                   128, 0)
+    rng = np.random.default_rng(5)
+    rows = np.sort(rng.choice(N, size=128, replace=False))
+    toks = np.sort(rng.choice(M, size=64, replace=False))
+    W_rows, B_rows, g_rows, _ = _oracle_rows(L, N, K, rows)
     g = torch.Generator(device="cuda")
     g.manual_seed(4)
     x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
     h = S.lora_h(L, x)
     y = S.forward(L, x, h=h)
-    ref = (x.float() @ W.float().t() + L.lora_scale * (h @ L.lora_B.float().t())) * L.dora_gamma.float()
-    e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
+    ref = O.forward_f64(W_rows, x.float().cpu().numpy()[toks], h.cpu().numpy()[toks], B_rows, g_rows, L.lora_scale)
+    e = rel_err(y.float().cpu().numpy()[toks][:, rows], ref)
     assert e <= 2e-2, (name, M, e)
 
 
@@ -120,20 +131,22 @@ def test_decode_batch_17_to_32(name, M):
     """Decode batches of 17..32 tokens at BASELINE shapes through wlq_gemm:
     the GEMV-class kernel (four 8-token MMA tiles) where the tensor-core
     GEMM would not fill the device (qkv, o, down), the GEMM otherwise
-    (gate_up); against the dequantised weights in fp32."""
+    (gate_up); against the oracle's float64 forward on 512 sampled rows over
+    the full K, h given and h computed in the kernel."""
     from qwen_wlqfastshot_helen_beta_b200 import synthetic as S
     K, N = S.QWEN25_7B[name]
     L = S.make_layer(N, K, group_size=128, density=0.005, r=16, seed=21).prepack(torch.bfloat16)
-    W = torch.empty((N, K), dtype=torch.float16, device="cuda")
-    C().dequant_w0(L.q_packed, L.lut_c, W, N, K, 4, L.words_per_row, L.chunk_offsets, L.chunk_cols, L.chunk_vals,
-                   128, 0)
+    rows = np.sort(np.random.default_rng(6).choice(N, size=512, replace=False))
+    W_rows, B_rows, g_rows, A64 = _oracle_rows(L, N, K, rows)
     g = torch.Generator(device="cuda")
     g.manual_seed(6)
     x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
     h = S.lora_h(L, x)
-    ref = (x.float() @ W.float().t() + L.lora_scale * (h @ L.lora_B.float().t())) * L.dora_gamma.float()
-    for y in (S.forward(L, x, h=h), S.forward_fold(L, x)):
-        e = (y.float() - ref).abs().max().item() / ref.abs().max().item()
+    xf = x.float().cpu().numpy()
+    ref_h = O.forward_f64(W_rows, xf, h.cpu().numpy(), B_rows, g_rows, L.lora_scale)
+    ref_f = O.forward_f64(W_rows, xf, xf.astype(np.float64) @ A64.T, B_rows, g_rows, L.lora_scale)
+    for y, ref in ((S.forward(L, x, h=h), ref_h), (S.forward_fold(L, x), ref_f)):
+        e = rel_err(y.float().cpu().numpy()[:, rows], ref)
         assert e <= 2e-2, (name, M, e)
 
 
