@@ -176,3 +176,27 @@ def test_host_dequant_grouped_against_oracle():
         _C.dequant_w0(torch.from_numpy(q.view(np.int32)), torch.from_numpy(lut), W, N, K, 4, wpr,
                       torch.from_numpy(off), torch.from_numpy(cols), torch.from_numpy(vals), G, goff)
         assert np.array_equal(W.numpy().view(np.uint16), ref.view(np.uint16)), (N, K, G, goff)
+
+
+def test_tp_buffer_bytes_hold_the_packed_slots():
+    """wlq_tp_buffer_bytes: an error word, one call counter per 16-row tile,
+    then per parity, source rank and token a row of 8-byte words holding
+    every tile's eight words (two 16-bit values and a 32-bit epoch each, two
+    words per 16-byte store): the row is even and at least 8 words per tile,
+    also for widths below 16 rows."""
+    from qwen_wlqfastshot_helen_beta_b200 import _lib
+
+    def up(v, a):
+        return (v + a - 1) // a * a
+
+    for world in (2, 4, 8):
+        for max_N in (1, 3, 15, 16, 17, 100, 256, 3584, 18944, 37888):
+            tiles = (max_N + 15) // 16
+            stride = up(max(max_N, 8 * tiles), 2)
+            data = up(128 + 4 * tiles, 256)
+            want = up(data + 2 * world * 16 * stride * 8, 256)
+            got = int(_lib.lib.wlq_tp_buffer_bytes(world, max_N))
+            assert got == want, (world, max_N, got, want)
+            # the last word of the last tile of the last row lies inside
+            last = data + 8 * ((2 * world * 16 - 1) * stride + tiles * 8 - 1)
+            assert last + 8 <= got
