@@ -47,44 +47,46 @@ def _act_dtype(t: torch.Tensor) -> int:
     raise RuntimeError(f"wlq: activations must be float16 or bfloat16, got {t.dtype}")
 
 
-def _require(cond: bool, msg: str) -> None:
+def _require(cond: bool, msg) -> None:
+    """Raises with `msg` (a string, or a callable that formats it: checks on
+    the per-call path format their message only when they fail)."""
     if not cond:
-        raise RuntimeError(f"wlq: {msg}")
+        raise RuntimeError(f"wlq: {msg() if callable(msg) else msg}")
 
 
 def _check_common(name, tensors, required):
     for nm, t in zip(required, tensors):
-        _require(t is not None, f"{name}: {nm} is required")
-        _require(t.is_cuda, f"{name}: {nm} must be a CUDA tensor")
-        _require(t.is_contiguous(), f"{name}: {nm} must be contiguous")
+        _require(t is not None, lambda: f"{name}: {nm} is required")
+        _require(t.is_cuda, lambda: f"{name}: {nm} must be a CUDA tensor")
+        _require(t.is_contiguous(), lambda: f"{name}: {nm} must be contiguous")
 
 
 def _check_opt(name, nm, t, dtype, device):
     if t is None:
         return
-    _require(t.is_cuda and t.device == device, f"{name}: {nm} must be on {device}")
-    _require(t.is_contiguous(), f"{name}: {nm} must be contiguous")
-    _require(t.dtype == dtype, f"{name}: {nm} must be {dtype}, got {t.dtype}")
+    _require(t.is_cuda and t.device == device, lambda: f"{name}: {nm} must be on {device}")
+    _require(t.is_contiguous(), lambda: f"{name}: {nm} must be contiguous")
+    _require(t.dtype == dtype, lambda: f"{name}: {nm} must be {dtype}, got {t.dtype}")
 
 
 def _linear_checks(name, x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, vals, lora_B, lora_h, gamma,
                    group_size, group_offset, lut_format=WLQ_LUT_F16, lora_A=None):
     _check_common(name, (q_packed, lut_c, x, out), ("q_packed", "lut_c", "x", "out"))
-    _require(bits == 4, f"{name}: the fused kernels read 4-bit indices only (bits={bits})")
+    _require(bits == 4, lambda: f"{name}: the fused kernels read 4-bit indices only (bits={bits})")
     dev = x.device
     for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("out", out)):
-        _require(t.device == dev, f"{name}: {nm} must be on {dev}")
-    _require(q_packed.dtype == torch.int32, f"{name}: q_packed must be int32")
-    _require(lut_c.dtype == torch.float16, f"{name}: lut_c must be float16")
-    _require(out.dtype == x.dtype, f"{name}: out dtype {out.dtype} must match x dtype {x.dtype}")
-    _require(K > 0 and x.numel() % K == 0, f"{name}: x has {x.numel()} elements, not a multiple of K={K}")
+        _require(t.device == dev, lambda: f"{name}: {nm} must be on {dev}")
+    _require(q_packed.dtype == torch.int32, lambda: f"{name}: q_packed must be int32")
+    _require(lut_c.dtype == torch.float16, lambda: f"{name}: lut_c must be float16")
+    _require(out.dtype == x.dtype, lambda: f"{name}: out dtype {out.dtype} must match x dtype {x.dtype}")
+    _require(K > 0 and x.numel() % K == 0, lambda: f"{name}: x has {x.numel()} elements, not a multiple of K={K}")
     M = x.numel() // K
-    _require(out.numel() == M * N, f"{name}: out has {out.numel()} elements, expected {M}x{N}")
-    _require(q_packed.numel() >= N * wpr, f"{name}: q_packed has {q_packed.numel()} words, need {N}x{wpr}")
+    _require(out.numel() == M * N, lambda: f"{name}: out has {out.numel()} elements, expected {M}x{N}")
+    _require(q_packed.numel() >= N * wpr, lambda: f"{name}: q_packed has {q_packed.numel()} words, need {N}x{wpr}")
     ng = (K + group_offset + group_size - 1) // group_size if group_size > 0 else 1
     kcb = 1 << bits
     _require(lut_c.numel() == N * ng * kcb,
-             f"{name}: lut_c has {lut_c.numel()} entries, expected {N}x{ng}x{kcb} (group_size={group_size})")
+             lambda: f"{name}: lut_c has {lut_c.numel()} entries, expected {N}x{ng}x{kcb} (group_size={group_size})")
     if offs is not None and cols is not None and vals is not None:
         chunk_m = 640 if bits == 3 else 512
         nc = (K + chunk_m - 1) // chunk_m
@@ -93,22 +95,22 @@ def _linear_checks(name, x, q_packed, lut_c, out, N, K, bits, wpr, offs, cols, v
         _check_opt(name, "chunk_cols", cols, torch.int32 if lut_format == WLQ_LUT_PREPACKED else torch.uint16, dev)
         # prepacked layers carry float32 corrections in place of e5m2 bytes
         _check_opt(name, "chunk_vals", vals, torch.float32 if lut_format == WLQ_LUT_PREPACKED else torch.uint8, dev)
-        _require(offs.numel() == N * (nc + 1), f"{name}: chunk_offsets must be [{N}, {nc + 1}]")
-        _require(cols.numel() == vals.numel(), f"{name}: chunk_cols and chunk_vals lengths differ")
+        _require(offs.numel() == N * (nc + 1), lambda: f"{name}: chunk_offsets must be [{N}, {nc + 1}]")
+        _require(cols.numel() == vals.numel(), lambda: f"{name}: chunk_cols and chunk_vals lengths differ")
     r = 0
-    _require(lora_h is None or lora_A is None, f"{name}: give lora_h or lora_A, not both")
+    _require(lora_h is None or lora_A is None, lambda: f"{name}: give lora_h or lora_A, not both")
     if lora_B is not None and (lora_h is not None or lora_A is not None) and gamma is not None:
         _check_opt(name, "lora_B", lora_B, torch.float16, dev)
         _check_opt(name, "dora_gamma", gamma, torch.float16, dev)
         r = int(lora_B.size(1)) if lora_B.dim() > 1 else 0
-        _require(lora_B.numel() == N * r, f"{name}: lora_B must be [{N}, r]")
-        _require(gamma.numel() == N, f"{name}: dora_gamma must have {N} values")
+        _require(lora_B.numel() == N * r, lambda: f"{name}: lora_B must be [{N}, r]")
+        _require(gamma.numel() == N, lambda: f"{name}: dora_gamma must have {N} values")
         if lora_h is not None:
             _check_opt(name, "lora_h", lora_h, torch.float32, dev)
-            _require(lora_h.numel() == M * r, f"{name}: lora_h must hold {M}x{r} values")
+            _require(lora_h.numel() == M * r, lambda: f"{name}: lora_h must hold {M}x{r} values")
         else:
             _check_opt(name, "lora_A", lora_A, x.dtype, dev)  # A in the activation type
-            _require(lora_A.numel() == r * K, f"{name}: lora_A must be [{r}, {K}]")
+            _require(lora_A.numel() == r * K, lambda: f"{name}: lora_A must be [{r}, {K}]")
     return M, r
 
 
@@ -164,14 +166,14 @@ def lora_h(x, lora_A, out=None):
     _check_common("lora_h", (x, lora_A), ("x", "lora_A"))
     _require(lora_A.dim() == 2, "lora_h: lora_A must be [r, K]")
     r, K = int(lora_A.shape[0]), int(lora_A.shape[1])
-    _require(lora_A.dtype == x.dtype, f"lora_h: lora_A dtype {lora_A.dtype} must match x dtype {x.dtype}")
-    _require(lora_A.device == x.device, f"lora_h: lora_A must be on {x.device}")
-    _require(K > 0 and x.numel() % K == 0, f"lora_h: x has {x.numel()} elements, not a multiple of K={K}")
+    _require(lora_A.dtype == x.dtype, lambda: f"lora_h: lora_A dtype {lora_A.dtype} must match x dtype {x.dtype}")
+    _require(lora_A.device == x.device, lambda: f"lora_h: lora_A must be on {x.device}")
+    _require(K > 0 and x.numel() % K == 0, lambda: f"lora_h: x has {x.numel()} elements, not a multiple of K={K}")
     M = x.numel() // K
     if out is None:
         out = torch.empty((M, r), dtype=torch.float32, device=x.device)
     _require(out.is_cuda and out.is_contiguous() and out.dtype == torch.float32 and out.numel() == M * r,
-             f"lora_h: out must be a contiguous float32 CUDA tensor of {M}x{r} values")
+             lambda: f"lora_h: out must be a contiguous float32 CUDA tensor of {M}x{r} values")
     with _DeviceGuard(x.device):
         rc = lib.wlq_lora_h(_ptr(x), _ptr(lora_A), _ptr(out), M, K, r, _act_dtype(x), _stream(x.device))
     check(rc, "wlq_lora_h")
@@ -305,7 +307,7 @@ def dequant_w0(q_packed, lut_c, W_out, N, K, bits, words_per_row, chunk_offsets,
         for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("chunk_offsets", offs), ("chunk_cols", cols),
                       ("chunk_vals", vals)):
             _require(t is None or (t.is_cuda and t.device == W_out.device and t.is_contiguous()),
-                     f"dequant_w0: {nm} must be a contiguous tensor on {W_out.device}")
+                     lambda: f"dequant_w0: {nm} must be a contiguous tensor on {W_out.device}")
         with _DeviceGuard(W_out.device):
             rc = lib.wlq_dequant(_ptr(q_packed), _ptr(lut_c), _ptr(W_out), _ptr(offs), _ptr(cols), _ptr(vals),
                                  N, K, bits, wpr, int(lut_group_size), int(lut_group_offset),
@@ -314,7 +316,7 @@ def dequant_w0(q_packed, lut_c, W_out, N, K, bits, words_per_row, chunk_offsets,
         return
     for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("chunk_offsets", offs), ("chunk_cols", cols),
                   ("chunk_vals", vals)):
-        _require(t is None or (not t.is_cuda and t.is_contiguous()), f"dequant_w0: {nm} must be a CPU tensor")
+        _require(t is None or (not t.is_cuda and t.is_contiguous()), lambda: f"dequant_w0: {nm} must be a CPU tensor")
     rc = lib.wlq_dequant_host(_ptr(q_packed), _ptr(lut_c), _ptr(W_out), _ptr(offs), _ptr(cols), _ptr(vals),
                               N, K, bits, wpr, int(lut_group_size), int(lut_group_offset))
     check(rc, "wlq_dequant_host")
@@ -349,7 +351,8 @@ def prepack_outliers(q_packed, lut_c, chunk_offsets, chunk_cols, chunk_vals, N, 
     dev = q_packed.device
     for nm, t in (("q_packed", q_packed), ("lut_c", lut_c), ("chunk_offsets", offs), ("chunk_cols", cols),
                   ("chunk_vals", vals)):
-        _require(t.is_cuda and t.device == dev and t.is_contiguous(), f"prepack_outliers: {nm} must be on {dev}")
+        _require(t.is_cuda and t.device == dev and t.is_contiguous(),
+                 lambda: f"prepack_outliers: {nm} must be on {dev}")
     _require(vals.dtype == torch.uint8 and cols.dtype == torch.uint16, "prepack_outliers: e5m2 bytes / uint16 cols")
     gcols = torch.empty(cols.numel(), dtype=torch.int32, device=dev)
     delta = torch.empty(cols.numel(), dtype=torch.float32, device=dev)
