@@ -1,4 +1,4 @@
-// Decode GEMV for M = 1..16 token rows over 4-bit LUT-quantised weights, with
+// Decode GEMV for M = 1..32 token rows over 4-bit LUT-quantised weights, with
 // outlier replacement and the DoRA epilogue fused.  Replaces
 // gemv_chunk_csr_kernel + reduce_split_k_dora_kernel
 // (csrc/gemv_kernel.cu:86-353) and, for 2 <= M <= 16, the wmma kernel
@@ -24,15 +24,21 @@
 //    registers or scoreboards, and a chunk is read with one 128-bit shared
 //    load per row;
 //  * the CTA stages its K range of the activations in shared memory once
-//    (cp.async) when it fits, so the B fragments are short-latency loads;
+//    (cp.async) when it fits, so the B fragments are short-latency loads:
+//    4-warp CTAs (4 per SM) where that fits beside their rings, else one
+//    16-warp CTA per SM that holds up to ~112 KB of activations for all its
+//    warps (also where neither shape splits K);
 //  * each warp owns a 16-row tile; K is split only across the CTAs of a
 //    thread-block cluster, whose partial tiles meet in distributed shared
-//    memory: no global workspace, no second launch.
-// Outliers REPLACE the codebook weight (csrc/gemm_kernel.cu:204-228).  After
-// the MMA loop each warp adds (w_outlier - w_codebook) * x for the outliers of
-// its tile (the arithmetic of csrc/gemv_kernel.cu:262-288): two lanes per row
-// walk the row's chunk-CSR entries, accumulate in registers and combine with
-// one shuffle.
+//    memory: no global workspace, no second launch;
+//  * with wlq_gemv_set_overlap on, a launch is a programmatic dependent
+//    launch: it reads only weights before griddepcontrol.wait.
+// Outliers REPLACE the codebook weight (csrc/gemm_kernel.cu:204-228).  Before
+// the MMA loop, so that its dependent loads overlap the ring's first chunks,
+// each warp adds (w_outlier - w_codebook) * x for the outliers of its tile
+// (the arithmetic of csrc/gemv_kernel.cu:262-288): two lanes per row walk the
+// row's chunk-CSR entries, accumulate in registers and combine with one
+// shuffle, seeding the warp's partial tile.
 #include <atomic>
 #include <mutex>
 #include <utility>
