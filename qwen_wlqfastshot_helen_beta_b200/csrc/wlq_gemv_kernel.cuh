@@ -234,11 +234,13 @@ __device__ void tp_allreduce_tile(const GemvParams& p, float (*part)[MT], uint32
     if (lane == 0) p.tp_counters[tile] = cnt;
 }
 
-// RT > 0: the low-rank input h = A x (r <= 16 RT) is computed here.  In
-// chunk c warp w multiplies its block A[:, 128c + 32w, +32), staged through
-// its ring, with the activations on the tensor core (A rows are the MMA's A
-// operand, tokens its B operand); after the main loop the four warps' partial
-// h meet in shared memory and each warp adds s B h for its rows.  With the K
+// RT > 0: the low-rank input h = A x (r <= 16 RT) is computed here.  Each
+// chunk's 128 columns are four 32-column blocks; a warp multiplies the blocks
+// it is assigned (all four warps of a 4-warp CTA take block w of every chunk;
+// see h_duty for 16 warps), staged through its ring, with the activations on
+// the tensor core (A rows are the MMA's A operand, tokens its B operand);
+// after the main loop the warps' partial h meet in shared memory and each
+// warp adds s B h for its rows.  With the K
 // range split over a cluster each rank adds the term for its own range, and
 // the split-K reduction sums them.
 template <typename T, int NT, int NSLOT, bool PREPACKED, bool XVEC, bool XSMEM, int S, int RT, int WARPS>
@@ -740,8 +742,8 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_kernel(const Gemv
             chunk(c, base, BoolTag<false>{});
     }
     if constexpr (RT > 0) {
-        // the four warps' partial h [16 RT][MT] meet in their (now idle)
-        // rings; each warp then adds s B h for its rows, h in the MMA type
+        // the warps' partial h [16 RT][MT] meet in their (now idle) rings;
+        // each warp then adds s B h for its rows, h in the MMA type
         __syncwarp();  // every lane's last ring reads are done
         float* hmine = reinterpret_cast<float*>(smem + p.x_bytes + warp * S * R::kStageBytes);
 #pragma unroll
